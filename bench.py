@@ -1,0 +1,340 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 layer-stack forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C3] [--impl tk|reference]
+
+A "step" is one forward of the layer stack over one synthetic batch of the
+chosen configuration (default C3: batch 256, seq 256, d_model 1024, 16
+heads, ffn 4096, 4 layers, bidirectional -- the large-batch GEMM regime that
+BASELINE.json runs at 1/2/4/8 GPUs). Weights are the harness's default
+initialisation under torch.manual_seed(0); x ~ N(0, 1) fp32, seeded on the
+CPU. Batch rows are independent, so under torchrun every rank runs its own
+full batch on its own GPU with no data-path collective (weak scaling); the
+value is all ranks' tokens over the max-over-ranks device time.
+
+Metric: tokens/s (= B*S*1000 / ms per forward, the harness's throughput,
+src/torch_transformer_benchmark.py:565-567). ``value`` is device-timed with
+inputs resident in HBM (inputs are > L2, so no flush is needed); ``e2e``
+times the same forward through the public API with the input copied from
+pinned host memory and the fp32 output copied back every step.
+
+``--impl reference`` times the fp32 CPU forward of the reference model (the
+oracle's restatement of BaselineTransformer; the reference is pure Python
+and does not travel to the GPU box) on the host cores, one bounded
+batch-slice per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PKG = ROOT / "transformer-kernel_b200"
+for p in (str(ROOT), str(PKG)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import torch  # noqa: E402
+
+# name: (B, S, d, H, ffn, L, causal)
+CONFIGS = {
+    "C1": (64, 128, 128, 4, 128, 4, True),
+    "C2": (1, 512, 512, 8, 2048, 4, True),
+    "C3": (256, 256, 1024, 16, 4096, 4, False),
+    "C4": (8, 8192, 1024, 16, 4096, 2, True),
+}
+METRIC = "layer-stack forward tokens/s"
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        m = json.loads(path.read_text())
+        return m["hbm_gbs"], m["bf16_tflops"], m["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def gemm_flops(T, d, ffn):
+    return {"gemm_qkv": 2 * T * d * 3 * d, "gemm_o": 2 * T * d * d, "gemm_o_ln": 2 * T * d * d,
+            "gemm_ffn_in": 2 * T * d * ffn, "gemm_ffn_out": 2 * T * ffn * d, "gemm_ffn_out_ln": 2 * T * ffn * d}
+
+
+def attn_flops(B, S, H, hd, causal):
+    pairs = S * (S + 1) / 2 if causal else S * S
+    return 4 * B * H * pairs * hd
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons with nvidia-smi while timing."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def cpu_forward_rate(cfg_tuple, seconds, sample_batch, steps=None):
+    """Oracle (fp32 CPU BaselineTransformer restatement) tokens/s on a
+    batch slice. Returns (tokens_per_s, threads, description)."""
+    from oracle import StackConfig, generate_random_case, init_params, stack_forward
+
+    B, S, d, H, ffn, L, causal = cfg_tuple
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    nb = min(B, sample_batch)
+    cfg = StackConfig(nb, S, d, H, ffn, L, causal)
+    params = init_params(cfg, seed=0)
+    x, mask = generate_random_case(cfg, seed=1234 + 100000)
+    stack_forward(params, cfg, x[:1], mask[:1])  # warm
+    times = []
+    t_end = time.perf_counter() + seconds
+    n = 0
+    while True:
+        t0 = time.perf_counter()
+        stack_forward(params, cfg, x, mask)
+        times.append(time.perf_counter() - t0)
+        n += 1
+        if (steps is not None and n >= steps) or (steps is None and time.perf_counter() >= t_end):
+            break
+    med = statistics.median(times)
+    return nb * S / med, threads, f"{nb} of {B} sequences x {n} forwards, median {med * 1e3:.1f} ms", times
+
+
+def run_reference(args, cfg_tuple, rank):
+    """--impl reference: the CPU fp32 reference forward on the host cores."""
+    if rank != 0:
+        return
+    B, S, d, H, ffn, L, causal = cfg_tuple
+    sample = 8 if args.config in ("C3",) else (1 if args.config == "C4" else B)
+    rate, threads, desc, times = cpu_forward_rate(cfg_tuple, 0, sample, steps=args.warmup + args.steps)
+    times = times[args.warmup:] or times
+    med = statistics.median(times)
+    value = min(B, sample) * S / med
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": med * 1e3 * (B / min(B, sample)), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
+                   "global_batch": B, "seq_len": S, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{min(B, sample)} of {B} sequences per step"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="C3", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="tk", choices=["tk", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg_tuple = CONFIGS[args.config]
+    B, S, d, H, ffn, L, causal = cfg_tuple
+
+    if args.impl == "reference":
+        run_reference(args, cfg_tuple, rank)
+        return 0
+
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import _tklib as tk
+    import optimized
+
+    ocfg = optimized.TransformerConfig(B, S, d, H, ffn, L, causal)
+    torch.manual_seed(0)
+    model = optimized.OptimizedTransformer(ocfg).to(dev).eval()
+    gen = torch.Generator().manual_seed(1234 + 100000)
+    x_host = torch.randn(B, S, d, generator=gen).pin_memory()
+    mask_host = torch.ones(B, S, dtype=torch.bool).pin_memory()
+    x = x_host.to(dev)
+    mask = mask_host.to(dev)
+    out_host = torch.empty(B, S, d, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.inference_mode():
+        # ---- device-resident timing ----
+        for _ in range(args.warmup):
+            model(x, mask)
+        tk.check_device_errors(dev)
+        barrier()
+        torch.cuda.synchronize(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            t0.record(stream)
+            for _ in range(args.steps):
+                model(x, mask)
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
+        barrier()
+        ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        clocks = clk.summary()
+        tk.check_device_errors(dev)
+
+        # ---- per-kernel event timing (separate pass, same stream) ----
+        trace = []
+        model.launch_trace = trace
+        for _ in range(args.steps):
+            model(x, mask)
+        torch.cuda.synchronize(dev)
+        model.launch_trace = None
+        per = {}
+        for name, a, b in trace:
+            per.setdefault(name, []).append(a.elapsed_time(b))
+        launches_per_step = len(trace) // args.steps
+
+        # ---- end to end: pinned host input -> forward -> host output ----
+        for _ in range(3):
+            x.copy_(x_host, non_blocking=True)
+            out_host.copy_(model(x, mask), non_blocking=True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            x.copy_(x_host, non_blocking=True)
+            out_host.copy_(model(x, mask), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    tokens = B * S
+    value = world * tokens * 1000.0 / ms
+    hbm, tf_burst, tf_sus, peak_kind = peaks()
+    # dominant kernel by total time
+    totals = {k: sum(v) for k, v in per.items()}
+    dom = max(totals, key=totals.get)
+    avg_ms = statistics.fmean(per[dom])
+    T = tokens
+    fl = gemm_flops(T, d, ffn)
+    if dom in fl:
+        achieved = fl[dom] / (avg_ms * 1e-3) / 1e12
+        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
+                "frac": achieved / tf_sus, "peak_kind": f"{peak_kind} bf16 sustained"}
+    elif dom == "attn":
+        achieved = attn_flops(B, S, H, d // H, causal) / (avg_ms * 1e-3) / 1e12
+        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
+                "frac": achieved / tf_sus, "peak_kind": f"{peak_kind} bf16 sustained"}
+    else:
+        achieved = T * d * (4 + 2) / (avg_ms * 1e-3) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                "frac": achieved / hbm, "peak_kind": f"{peak_kind} copy"}
+    roof["traffic"] = None
+    share = {k: round(v / sum(totals.values()), 4) for k, v in sorted(totals.items(), key=lambda kv: -kv[1])}
+    kernels_ms = {k: round(statistics.fmean(v), 5) for k, v in per.items()}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        sample = 8 if args.config == "C3" else (1 if args.config == "C4" else B)
+        rate, threads, desc, _ = cpu_forward_rate(cfg_tuple, args.cpu_seconds, sample)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16 operands / f32 accumulate+residual", "data": "synthetic",
+        "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
+                   "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world} (batch-sharded, no collective)",
+                   "l2": "inputs and activations > 126 MB L2; no flush"},
+        "e2e": {"value": world * tokens * 1000.0 / e2e_ms, "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 4},
+        "roofline": roof,
+        "kernel_ms": kernels_ms,
+        "kernel_share": share,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,140 @@
+/*
+ * libtk_b200 -- C ABI of the B200 (sm_100a) Transformer layer-stack forward.
+ *
+ * Plain pointers, 64-bit sizes and a cudaStream_t passed as void*; no torch
+ * types. The caller allocates and owns every buffer (device memory on the
+ * device that is current for the calling thread); the library keeps only a
+ * per-device error word and cached device properties. Every entry point
+ * returns TK_OK (0) or a negative tk_status; tk_last_error() then describes
+ * the failure (per calling thread). Calls are stream-ordered and do not
+ * synchronise, except tk_check_device_errors().
+ *
+ * Each declaration names the reference interface it replaces
+ * (danielfodgaard/transformer-kernel, file:line).
+ */
+#ifndef TK_B200_H_
+#define TK_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TK_API __attribute__((visibility("default")))
+#else
+#define TK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tk_status {
+  TK_OK = 0,
+  TK_ERR_INVALID = -1,      /* bad pointer / size / stride argument            */
+  TK_ERR_UNSUPPORTED = -2,  /* valid request outside the kernels' envelope     */
+  TK_ERR_LAUNCH = -3,       /* CUDA launch or tensor-map encode failed         */
+  TK_ERR_TIMEOUT = -4,      /* a device-side wait gave up (see tk_last_error)  */
+  TK_ERR_CUDA = -5,         /* other CUDA runtime error                        */
+  TK_ERR_DEVICE = -6        /* kernel reported an error through the error word */
+} tk_status;
+
+typedef enum tk_dtype { TK_F32 = 0, TK_F16 = 1 } tk_dtype;
+
+typedef enum tk_epilogue {
+  TK_EPI_BIAS = 0,          /* out16 = A W^T + b                                */
+  TK_EPI_BIAS_GELU = 1,     /* out16 = gelu_erf(A W^T + b)                      */
+  TK_EPI_BIAS_RESID = 2,    /* sum32 = resid + A W^T + b                        */
+  TK_EPI_BIAS_RESID_LN = 3  /* sum32 = resid + A W^T + b; out = LN(sum32)       */
+} tk_epilogue;
+
+/* Row LayerNorm, optionally fused with a residual add.
+ *   y == NULL : out = LN(x)                      -- replaces ln_fwd
+ *               (src/fused_kernels.py:164-193)
+ *   y != NULL : s = x + y (fp32 math, stored in x's dtype when sum_out is
+ *               non-NULL); out = LN(s)          -- replaces add_ln_fwd
+ *               (src/fused_kernels.py:196-238)
+ * Statistics in fp32 (mean, centred variance, rsqrt(var + eps)), then the
+ * affine, then the cast to out_dtype. x/y/out dtypes: TK_F32 or TK_F16;
+ * gamma/beta fp32 [d]. Rows are `ld_*` elements apart. 1 <= d <= 8192.
+ * row_len/seq_len: optional prefix-padding lengths (int32 [rows/seq_len]);
+ * rows whose position >= row_len[row/seq_len] get s = 0 and out = 0 (the
+ * harness's masked_fill of padded tokens, src/torch_transformer_benchmark.py:169-171). */
+TK_API int tk_layernorm(const void* x, int x_dtype, int64_t ld_x,
+                 const void* y, int y_dtype, int64_t ld_y,
+                 void* sum_out, int64_t ld_sum,
+                 const float* gamma, const float* beta, float eps,
+                 void* out, int out_dtype, int64_t ld_out,
+                 const int32_t* row_len, int64_t seq_len,
+                 int64_t rows, int64_t d, void* stream);
+
+/* out = epilogue(A[M,K] . W[N,K]^T + bias), fp16 operands, fp32 accumulate
+ * on the tcgen05 tensor cores. Replaces F.linear (src/optimized.py:572, :627,
+ * :632-636) plus the elementwise ops fused into its epilogue (GELU
+ * src/optimized.py:635; residual add + LayerNorm src/fused_kernels.py:196-238).
+ *   A     : fp16 [M, K], row stride lda (elements), lda % 8 == 0
+ *   W     : fp16 [N, K] (nn.Linear.weight as-is), row stride ldw, ldw % 8 == 0
+ *   bias  : fp32 [N]
+ *   TK_EPI_BIAS / _GELU : out fp16 [M, N], ldo % 8 == 0
+ *   TK_EPI_BIAS_RESID   : resid fp32 [M, N] (ld_resid), sum_out fp32 (ld_sum)
+ *   TK_EPI_BIAS_RESID_LN: as RESID, plus out = LN(sum) with gamma/beta fp32 [N],
+ *                         out_dtype TK_F16 or TK_F32; needs N in {64,128,256}
+ *   row_len/seq_len : optional prefix-padding lengths [M/seq_len]; rows whose
+ *                     position >= row_len[row/seq_len] are written as zeros
+ * N % 32 == 0 and K % 8 == 0. `resid` may alias `sum_out` (in-place). */
+TK_API int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw,
+            const float* bias, int epilogue,
+            const float* resid, int64_t ld_resid,
+            float* sum_out, int64_t ld_sum,
+            const float* gamma, const float* beta, float eps,
+            void* out, int out_dtype, int64_t ldo,
+            const int32_t* row_len, int64_t seq_len,
+            int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Attention forward. Replaces F.scaled_dot_product_attention
+ * (src/optimized.py:615-624) and flash_attention (src/kernels.py:250-294),
+ * with the same contract as the latter: q, k, v are fp16, logically
+ * [B, H, S, hd], with arbitrary strides (elements, shared by the three,
+ * multiples of 8) and a contiguous last dimension -- e.g. views into the
+ * fused [B, S, 3, H, hd] QKV projection (stride_b = 3*S*H*hd,
+ * stride_h = hd, stride_s = 3*H*hd). The output is written directly as
+ * [B, S, H*hd] fp16 with row stride ld_out (% 8 == 0).
+ *   scale  : multiplies q.k after the product (the harness uses hd**-0.5)
+ *   causal : mask keys j > query i
+ *   kv_len : optional int32 [B]; keys >= kv_len[b] are masked
+ * hd in {32, 64}. */
+TK_API int tk_attn_fwd(const void* q, const void* k, const void* v,
+                int64_t stride_b, int64_t stride_h, int64_t stride_s,
+                void* out, int64_t ld_out,
+                int64_t B, int64_t S, int64_t H, int64_t hd, float scale,
+                int causal, const int32_t* kv_len, void* stream);
+
+/* Guard probes, same meaning as the reference's can_fuse
+ * (src/fused_kernels.py:62-64) and attention_supported
+ * (src/kernels.py:96-103): 1 when the kernels accept the shape. */
+TK_API int tk_layernorm_supported(int64_t d);
+TK_API int tk_attn_supported(int64_t head_dim);
+
+/* Synchronise `stream`, then read and clear the current device's error word
+ * (set by kernels whose bounded waits gave up). TK_OK or TK_ERR_TIMEOUT /
+ * TK_ERR_DEVICE with a message in tk_last_error(). */
+TK_API int tk_check_device_errors(void* stream);
+
+/* Limit, in nanoseconds, of every device-side wait in later launches
+ * (default 2e9). Returns the previous value. */
+TK_API uint64_t tk_set_wait_limit_ns(uint64_t ns);
+
+/* Test hook for failure detection: launches one CTA that waits on an
+ * mbarrier nothing arrives on, with the configured limit, so the wait gives
+ * up and records TK_ERR_TIMEOUT in the error word. Never faults. */
+TK_API int tk_selftest_wait_timeout(void* stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+TK_API const char* tk_last_error(void);
+
+/* Library version string. */
+TK_API const char* tk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TK_B200_H_ */

@@ -1,0 +1,113 @@
+"""tk_gemm parity (GPU): every epilogue against an fp32 CPU reference on the
+same fp16-rounded operands. The GEMM accumulates exact fp16 products in
+fp32, so fp32 outputs agree to ~1e-4 relative and fp16 outputs to fp16
+rounding (atol 2e-3, rtol 2e-2, the reference's fp16 budget)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+import linear as tk_linear
+
+pytestmark = pytest.mark.gpu
+
+
+def seeded(*shape, seed=0, scale=1.0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(*shape, generator=g) * scale
+
+
+def operands(M, N, K, seed):
+    a = seeded(M, K, seed=seed).half()
+    w = (seeded(N, K, seed=seed + 1) * K ** -0.5).half()
+    b = seeded(N, seed=seed + 2) * 0.1
+    return a, w, b
+
+
+def ref_linear(a, w, b):
+    return a.float() @ w.float().t() + b
+
+
+# (M, N, K): model GEMM shapes of the configs (QKV, O, FFN-in, FFN-out), plus ragged M
+SHAPES = [
+    (8192, 384, 128), (8192, 128, 128),           # C1
+    (512, 1536, 512), (512, 512, 512), (512, 2048, 512), (512, 512, 2048),  # C2
+    (2048, 3072, 1024), (2048, 1024, 4096), (2048, 4096, 1024),            # C3/C4 (M cut)
+    (300, 256, 64), (129, 96, 200), (1, 64, 8),                            # ragged
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_bias(cuda_device, M, N, K):
+    a, w, b = operands(M, N, K, seed=M + N + K)
+    out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "bias")
+    torch.testing.assert_close(out.float().cpu(), ref_linear(a, w, b), atol=2e-3, rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 2048, 512), (2048, 4096, 1024), (129, 96, 200)])
+def test_gemm_bias_gelu(cuda_device, M, N, K):
+    a, w, b = operands(M, N, K, seed=7)
+    out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "gelu")
+    want = F.gelu(ref_linear(a, w, b), approximate="none")
+    torch.testing.assert_close(out.float().cpu(), want, atol=2e-3, rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 2048), (2048, 1024, 4096), (300, 256, 64), (129, 96, 200)])
+def test_gemm_bias_resid(cuda_device, M, N, K):
+    a, w, b = operands(M, N, K, seed=11)
+    r = seeded(M, N, seed=12)
+    s = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid", resid=r.cuda())
+    torch.testing.assert_close(s.cpu(), r + ref_linear(a, w, b), atol=1e-4, rtol=1e-4)
+
+
+def test_gemm_bias_resid_in_place(cuda_device):
+    a, w, b = operands(1024, 512, 512, seed=13)
+    r = seeded(1024, 512, seed=14)
+    buf = r.cuda()
+    s = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid", resid=buf, sum_out=buf)
+    assert s.data_ptr() == buf.data_ptr()
+    torch.testing.assert_close(buf.cpu(), r + ref_linear(a, w, b), atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("M,N,K", [(8192, 128, 128), (1000, 64, 256), (512, 256, 1024)])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_gemm_bias_resid_layernorm(cuda_device, M, N, K, out_dtype):
+    a, w, b = operands(M, N, K, seed=17)
+    r = seeded(M, N, seed=18)
+    g = seeded(N, seed=19, scale=0.5) + 1.0
+    beta = seeded(N, seed=20, scale=0.5)
+    s, h = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid_ln", resid=r.cuda(), ln_weight=g.cuda(),
+                            ln_bias=beta.cuda(), eps=1e-5, out_dtype=out_dtype)
+    want_s = r + ref_linear(a, w, b)
+    torch.testing.assert_close(s.cpu(), want_s, atol=1e-4, rtol=1e-4)
+    want_h = F.layer_norm(want_s, (N,), g, beta, 1e-5)
+    tol = dict(atol=2e-3, rtol=2e-2) if out_dtype == torch.float16 else dict(atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(h.float().cpu(), want_h, **tol)
+
+
+def test_gemm_row_len_zeroes_padded_rows(cuda_device):
+    S, B, N, K = 64, 3, 128, 128
+    a, w, b = operands(B * S, N, K, seed=23)
+    r = seeded(B * S, N, seed=24)
+    lengths = torch.tensor([64, 10, 1], dtype=torch.int32)
+    s, h = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid_ln", resid=r.cuda(),
+                            ln_weight=torch.ones(N).cuda(), ln_bias=torch.zeros(N).cuda(),
+                            out_dtype=torch.float32, row_len=lengths.cuda(), seq_len=S)
+    pos = torch.arange(B * S) % S
+    pad = pos >= lengths.repeat_interleave(S)
+    assert torch.all(s.cpu()[pad] == 0) and torch.all(h.cpu()[pad] == 0)
+    want_s = r + ref_linear(a, w, b)
+    torch.testing.assert_close(s.cpu()[~pad], want_s[~pad], atol=1e-4, rtol=1e-4)
+
+
+def test_gemm_output_guard_bands(cuda_device):
+    M, N, K, pad = 200, 96, 64, 4096
+    a, w, b = operands(M, N, K, seed=29)
+    buf = torch.full((M * N + 2 * pad,), 123.0, dtype=torch.float16, device="cuda")
+    out = buf[pad:pad + M * N].view(M, N)
+    tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "bias", out=out)
+    torch.cuda.synchronize()
+    assert torch.all(buf[:pad] == 123.0) and torch.all(buf[-pad:] == 123.0)
+    torch.testing.assert_close(out.float().cpu(), ref_linear(a, w, b), atol=2e-3, rtol=2e-2)

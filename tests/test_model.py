@@ -1,0 +1,119 @@
+"""Whole-stack parity (GPU): the B200 drop-in against the fp32 CPU oracle on
+the same seeded weights and inputs, under the harness's own acceptance rule
+(every element |u-r| <= 0.002 OR |u-r| <= 0.02*|r|,
+src/torch_transformer_benchmark.py:309-316, defaults :618-619)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import optimized
+from oracle import StackConfig, compare_outputs, generate_random_case, init_params, stack_forward
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 0.02, 0.002
+
+
+def build(cfg: StackConfig, **settings):
+    params = init_params(cfg, seed=0)
+    s = optimized.OptimizerSettings(**settings) if settings else None
+    model = optimized.OptimizedTransformer(cfg, s)
+    model.load_state_dict(params, strict=True)
+    return params, model.cuda().eval()
+
+
+def check(cfg, seeds, padding_ratio=0.0, **settings):
+    params, model = build(cfg, **settings)
+    worst = 0.0
+    for seed in seeds:
+        x, mask = generate_random_case(cfg, seed, padding_ratio)
+        ref = stack_forward(params, cfg, x, mask)
+        with torch.inference_mode():
+            out = model(x.cuda(), mask.cuda())
+        torch.cuda.synchronize()
+        assert out.shape == ref.shape and out.dtype == torch.float32
+        r = compare_outputs(ref, out.cpu(), RTOL, ATOL)
+        assert r.passed, f"seed {seed}: {r}"
+        worst = max(worst, r.max_abs_error)
+    return worst
+
+
+CONFIGS = {
+    "c1_b64_s128_d128": StackConfig(64, 128, 128, 4, 128, 4, True),
+    "c2_b1_s512_d512": StackConfig(1, 512, 512, 8, 2048, 4, True),
+    "c3_slice_b4_s256_d1024": StackConfig(4, 256, 1024, 16, 4096, 4, False),
+    "c4_slice_b1_s2048_d1024": StackConfig(1, 2048, 1024, 16, 4096, 2, True),
+    "small_d64_bidir": StackConfig(2, 16, 64, 2, 128, 2, False),
+    "ragged_s100_d128": StackConfig(2, 100, 128, 4, 256, 1, True),
+    "d256_hd64": StackConfig(2, 300, 256, 4, 512, 2, True),
+}
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+def test_stack_matches_oracle(cuda_device, name):
+    check(CONFIGS[name], seeds=[1234])
+
+
+def test_c1_five_harness_trials(cuda_device):
+    """The harness's accuracy loop: seeds seed+trial for 5 trials (:383-390)."""
+    worst = check(CONFIGS["c1_b64_s128_d128"], seeds=range(1234, 1239))
+    assert worst < ATOL
+
+
+def test_c1_against_reference_golden_rows(cuda_device, golden):
+    entry = golden["c1_reference_case1"]
+    cfg = StackConfig(**entry["config"])
+    _, model = build(cfg)
+    x, mask = generate_random_case(cfg, entry["input_seed"])
+    with torch.inference_mode():
+        out = model(x.cuda(), mask.cuda()).cpu()
+    got = torch.stack([out[i, j] for i, j in entry["out_rows_index"]])
+    assert compare_outputs(entry["out_rows"], got, RTOL, ATOL).passed
+
+
+@pytest.mark.parametrize("cfg", [StackConfig(3, 24, 64, 2, 128, 2, True), StackConfig(4, 200, 512, 8, 1024, 2, True),
+                                 StackConfig(2, 130, 128, 4, 128, 2, False)])
+def test_padded_prefix_masks(cuda_device, cfg):
+    check(cfg, seeds=[1236, 1237], padding_ratio=0.3)
+
+
+def test_fused_and_unfused_layernorm_paths_agree(cuda_device):
+    cfg = CONFIGS["c1_b64_s128_d128"]
+    _, fused = build(cfg, fused_ln_epilogue=True)
+    _, plain = build(cfg, fused_ln_epilogue=False)
+    x, mask = generate_random_case(cfg, 99)
+    with torch.inference_mode():
+        a = fused(x.cuda(), mask.cuda())
+        b = plain(x.cuda(), mask.cuda())
+    torch.testing.assert_close(a, b, atol=1e-3, rtol=0)
+
+
+def test_state_dict_keys_match_harness(cuda_device, golden):
+    cfg = StackConfig(**golden["c1_reference_case1"]["config"])
+    model = optimized.OptimizedTransformer(cfg)
+    assert list(model.state_dict().keys()) == golden["c1_reference_case1"]["weight_keys"]
+
+
+def test_non_prefix_mask_is_rejected(cuda_device):
+    import _tklib as tk
+
+    cfg = StackConfig(2, 32, 64, 2, 128, 1, True)
+    _, model = build(cfg)
+    x = torch.randn(2, 32, 64, device="cuda")
+    mask = torch.ones(2, 32, dtype=torch.bool, device="cuda")
+    mask[1, 3] = False
+    with pytest.raises(tk.TKError):
+        model(x, mask)
+
+
+def test_batch_rows_are_independent(cuda_device):
+    """Sharding by batch is exact: a slice of the batch gives the same rows."""
+    cfg = StackConfig(8, 256, 256, 4, 512, 2, True)
+    _, model = build(cfg)
+    x, mask = generate_random_case(cfg, 5)
+    with torch.inference_mode():
+        full = model(x.cuda(), mask.cuda())
+        part = model(x[2:5].cuda(), mask[2:5].cuda())
+    torch.testing.assert_close(full[2:5], part, atol=0, rtol=0)

@@ -1,0 +1,422 @@
+// C ABI of libtk_b200: argument checks, TMA tensor-map encoding, launch
+// configuration, and the device error word. One translation unit holds all
+// kernels so they share the error word (tk::g_error).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "tk_attn.cuh"
+#include "tk_gemm.cuh"
+#include "tk_layernorm.cuh"
+#include "tk_ptx.cuh"
+#include "../../include/tk_b200.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorLaunchFailure || e == cudaErrorInvalidConfiguration ? TK_ERR_LAUNCH : TK_ERR_CUDA,
+              "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// --- driver entry point for cuTensorMapEncodeTiled (no -lcuda needed) --------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// fp16 tensor map over a row-major matrix: dims innermost first.
+int make_map_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                 const cuuint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(TK_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TK_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return TK_OK;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  bool gemm_attr_set[4][4] = {};
+  bool attn_attr_set[2] = {};
+};
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+int current_device(int* dev, DeviceInfo** info) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= 64) return fail(TK_ERR_CUDA, "device ordinal %d out of range", *dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[*dev];
+  if (d.sms == 0) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, *dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, *dev);
+    if (major != 10 || minor != 0)
+      return fail(TK_ERR_UNSUPPORTED, "libtk_b200 is built for sm_100a; device %d is sm_%d%d", *dev, major, minor);
+    e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, *dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  }
+  *info = &d;
+  return TK_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ----------------------------------------------------------------------------
+// GEMM dispatch
+// ----------------------------------------------------------------------------
+template <int BN, int EPI>
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mw, const tk::gemm::Params& p, DeviceInfo* info,
+                cudaStream_t stream) {
+  using C = tk::gemm::Cfg<BN>;
+  auto kern = tk::gemm::gemm_kernel<BN, EPI>;
+  const int bi = BN == 64 ? 0 : BN == 128 ? 1 : 2;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!info->gemm_attr_set[bi][EPI]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm smem)");
+      info->gemm_attr_set[bi][EPI] = true;
+    }
+  }
+  const int tiles = ((p.M + tk::gemm::kBM - 1) / tk::gemm::kBM) * ((p.N + BN - 1) / BN);
+  const int grid = tiles < info->sms ? tiles : info->sms;
+  kern<<<grid, tk::gemm::kThreads, C::SMEM_BYTES, stream>>>(ma, mw, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
+  return TK_OK;
+}
+
+template <int BN>
+int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mw, const tk::gemm::Params& p,
+                    DeviceInfo* info, cudaStream_t s) {
+  switch (epi) {
+    case TK_EPI_BIAS: return launch_gemm<BN, tk::gemm::kBias>(ma, mw, p, info, s);
+    case TK_EPI_BIAS_GELU: return launch_gemm<BN, tk::gemm::kBiasGelu>(ma, mw, p, info, s);
+    case TK_EPI_BIAS_RESID: return launch_gemm<BN, tk::gemm::kBiasResid>(ma, mw, p, info, s);
+    case TK_EPI_BIAS_RESID_LN: return launch_gemm<BN, tk::gemm::kBiasResidLn>(ma, mw, p, info, s);
+  }
+  return fail(TK_ERR_INVALID, "unknown epilogue %d", epi);
+}
+
+// Tile width: the fused-LN epilogue needs the whole row in one tile; else the
+// widest tile that still gives every SM at least one tile.
+int pick_bn(int epi, int64_t M, int64_t N, int sms) {
+  if (epi == TK_EPI_BIAS_RESID_LN) return static_cast<int>(N);
+  const int64_t m_tiles = (M + 127) / 128;
+  for (int bn : {256, 128}) {
+    if (N % bn == 0 && m_tiles * (N / bn) >= sms) return bn;
+  }
+  return N % 32 == 0 ? 64 : 0;  // a 64-wide tile masks a trailing half tile
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tk_last_error(void) { return g_last_error.c_str(); }
+
+const char* tk_version(void) { return "tk_b200 0.1 (sm_100a)"; }
+
+uint64_t tk_set_wait_limit_ns(uint64_t ns) { return g_wait_limit_ns.exchange(ns); }
+
+int tk_layernorm_supported(int64_t d) { return d >= 1 && d <= 8192 ? 1 : 0; }
+
+int tk_attn_supported(int64_t head_dim) { return head_dim == 32 || head_dim == 64 ? 1 : 0; }
+
+int tk_layernorm(const void* x, int x_dtype, int64_t ld_x, const void* y, int y_dtype, int64_t ld_y, void* sum_out,
+                 int64_t ld_sum, const float* gamma, const float* beta, float eps, void* out, int out_dtype,
+                 int64_t ld_out, const int32_t* row_len, int64_t seq_len, int64_t rows, int64_t d, void* stream) {
+  g_last_error.clear();
+  if (rows < 0 || d < 1) return fail(TK_ERR_INVALID, "tk_layernorm: rows=%lld d=%lld", (long long)rows, (long long)d);
+  if (!tk_layernorm_supported(d)) return fail(TK_ERR_UNSUPPORTED, "tk_layernorm: d=%lld > 8192", (long long)d);
+  if (x == nullptr || gamma == nullptr || beta == nullptr || out == nullptr)
+    return fail(TK_ERR_INVALID, "tk_layernorm: null pointer");
+  if (sum_out != nullptr && y == nullptr) return fail(TK_ERR_INVALID, "tk_layernorm: sum_out needs y");
+  auto dt_ok = [](int t) { return t == TK_F32 || t == TK_F16; };
+  if (!dt_ok(x_dtype) || !dt_ok(out_dtype) || (y != nullptr && !dt_ok(y_dtype)))
+    return fail(TK_ERR_INVALID, "tk_layernorm: dtype must be TK_F32 or TK_F16");
+  if (ld_x < d || ld_out < d || (y != nullptr && ld_y < d) || (sum_out != nullptr && ld_sum < d))
+    return fail(TK_ERR_INVALID, "tk_layernorm: row stride smaller than d");
+  if (row_len != nullptr && (seq_len <= 0 || rows % seq_len != 0))
+    return fail(TK_ERR_INVALID, "tk_layernorm: row_len needs seq_len dividing rows");
+  if (rows == 0) return TK_OK;
+  int dev;
+  DeviceInfo* info;
+  if (int st = current_device(&dev, &info)) return st;
+
+  tk::ln::Args a;
+  a.row_len = row_len;
+  a.seq_len = seq_len > 0 ? seq_len : 1;
+  a.x = x; a.y = y; a.s = sum_out; a.gamma = gamma; a.beta = beta; a.h = out;
+  a.rows = rows; a.d = d; a.ld_x = ld_x; a.ld_y = ld_y; a.ld_s = ld_sum; a.ld_h = ld_out; a.eps = eps;
+  auto vec_ok = [&](const void* p, int64_t ld, int t) {
+    const size_t es = t == TK_F32 ? 4 : 2;
+    return p == nullptr || (aligned(p, 4 * es) && (ld * es) % (4 * es) == 0);
+  };
+  a.vec = (d % 4 == 0) && vec_ok(x, ld_x, x_dtype) && vec_ok(out, ld_out, out_dtype) &&
+          (y == nullptr || vec_ok(y, ld_y, y_dtype)) && (sum_out == nullptr || vec_ok(sum_out, ld_sum, x_dtype)) &&
+          aligned(gamma, 16) && aligned(beta, 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool xf = x_dtype == TK_F32, yf = (y == nullptr) || y_dtype == TK_F32, of = out_dtype == TK_F32;
+
+#define TK_LN_DISPATCH(KERNEL, GRID, ...)                                                         \
+  do {                                                                                          \
+    if (xf && yf && of) KERNEL<__VA_ARGS__ float, float, float, float><<<GRID, 256, 0, s>>>(a);  \
+    else if (xf && yf && !of) KERNEL<__VA_ARGS__ float, float, float, __half><<<GRID, 256, 0, s>>>(a); \
+    else if (xf && !yf && of) KERNEL<__VA_ARGS__ float, __half, float, float><<<GRID, 256, 0, s>>>(a); \
+    else if (xf && !yf && !of) KERNEL<__VA_ARGS__ float, __half, float, __half><<<GRID, 256, 0, s>>>(a); \
+    else if (!xf && yf && of) KERNEL<__VA_ARGS__ __half, float, __half, float><<<GRID, 256, 0, s>>>(a); \
+    else if (!xf && yf && !of) KERNEL<__VA_ARGS__ __half, float, __half, __half><<<GRID, 256, 0, s>>>(a); \
+    else if (!xf && !yf && of) KERNEL<__VA_ARGS__ __half, __half, __half, float><<<GRID, 256, 0, s>>>(a); \
+    else KERNEL<__VA_ARGS__ __half, __half, __half, __half><<<GRID, 256, 0, s>>>(a);              \
+  } while (0)
+
+  if (d <= 1024) {
+    const int64_t warps_needed = rows;
+    int64_t blocks = (warps_needed + 7) / 8;
+    const int64_t cap = static_cast<int64_t>(info->sms) * 16;
+    const int grid = static_cast<int>(blocks < cap ? blocks : cap);
+    if (d <= 128) TK_LN_DISPATCH(tk::ln::ln_warp_rows, grid, 1,);
+    else if (d <= 256) TK_LN_DISPATCH(tk::ln::ln_warp_rows, grid, 2,);
+    else if (d <= 512) TK_LN_DISPATCH(tk::ln::ln_warp_rows, grid, 4,);
+    else TK_LN_DISPATCH(tk::ln::ln_warp_rows, grid, 8,);
+  } else {
+    const int64_t cap = static_cast<int64_t>(info->sms) * 8;
+    const int grid = static_cast<int>(rows < cap ? rows : cap);
+    TK_LN_DISPATCH(tk::ln::ln_cta_rows, grid, );
+  }
+#undef TK_LN_DISPATCH
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tk_layernorm launch");
+  return TK_OK;
+}
+
+int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, int epilogue,
+            const float* resid, int64_t ld_resid, float* sum_out, int64_t ld_sum, const float* gamma,
+            const float* beta, float eps, void* out, int out_dtype, int64_t ldo, const int32_t* row_len,
+            int64_t seq_len, int64_t M, int64_t N, int64_t K, void* stream) {
+  g_last_error.clear();
+  if (A == nullptr || W == nullptr || bias == nullptr) return fail(TK_ERR_INVALID, "tk_gemm: null A/W/bias");
+  if (M < 0 || N <= 0 || K <= 0 || M > (1ll << 31) - 1 || N > 65536 || K > 65536)
+    return fail(TK_ERR_INVALID, "tk_gemm: bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (N % 32 != 0 || K % 8 != 0)
+    return fail(TK_ERR_UNSUPPORTED, "tk_gemm: needs N %% 32 == 0 and K %% 8 == 0 (N=%lld K=%lld)", (long long)N,
+                (long long)K);
+  if (lda < K || ldw < K || lda % 8 != 0 || ldw % 8 != 0 || !aligned(A, 16) || !aligned(W, 16))
+    return fail(TK_ERR_INVALID, "tk_gemm: A/W need 16-byte aligned rows (ld %% 8 == 0, ld >= K)");
+  if (!aligned(bias, 16)) return fail(TK_ERR_INVALID, "tk_gemm: bias must be 16-byte aligned");
+  const bool resid_epi = epilogue == TK_EPI_BIAS_RESID || epilogue == TK_EPI_BIAS_RESID_LN;
+  if (resid_epi) {
+    if (resid == nullptr || sum_out == nullptr || ld_resid < N || ld_sum < N || ld_resid % 4 || ld_sum % 4 ||
+        !aligned(resid, 16) || !aligned(sum_out, 16))
+      return fail(TK_ERR_INVALID, "tk_gemm: residual epilogue needs 16-byte aligned fp32 resid/sum_out rows");
+  }
+  const bool ln_epi = epilogue == TK_EPI_BIAS_RESID_LN;
+  if (ln_epi) {
+    if (gamma == nullptr || beta == nullptr || !aligned(gamma, 16) || !aligned(beta, 16))
+      return fail(TK_ERR_INVALID, "tk_gemm: LN epilogue needs aligned gamma/beta");
+    if (!(N == 64 || N == 128 || N == 256))
+      return fail(TK_ERR_UNSUPPORTED, "tk_gemm: fused LN epilogue needs N in {64,128,256} (N=%lld)", (long long)N);
+  }
+  const bool writes_out = epilogue != TK_EPI_BIAS_RESID;
+  if (writes_out) {
+    const bool f32 = ln_epi && out_dtype == TK_F32;
+    if (!ln_epi && out_dtype != TK_F16) return fail(TK_ERR_INVALID, "tk_gemm: this epilogue writes fp16");
+    if (out == nullptr || ldo < N || (f32 ? ldo % 4 : ldo % 8) != 0 || !aligned(out, 16))
+      return fail(TK_ERR_INVALID, "tk_gemm: out needs 16-byte aligned rows");
+  }
+  if (row_len != nullptr && (seq_len <= 0 || M % seq_len != 0))
+    return fail(TK_ERR_INVALID, "tk_gemm: row_len needs seq_len dividing M");
+  if (M == 0) return TK_OK;
+  int dev;
+  DeviceInfo* info;
+  if (int st = current_device(&dev, &info)) return st;
+  const int bn = pick_bn(epilogue, M, N, info->sms);
+  if (bn == 0) return fail(TK_ERR_UNSUPPORTED, "tk_gemm: N=%lld has no tile width", (long long)N);
+
+  CUtensorMap ma, mw;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(lda) * 2};
+    cuuint32_t box[2] = {64, 128};
+    if (int st = make_map_f16(&ma, A, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldw) * 2};
+    cuuint32_t box[2] = {64, static_cast<cuuint32_t>(bn)};
+    if (int st = make_map_f16(&mw, W, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  tk::gemm::Params p;
+  p.M = static_cast<int>(M); p.N = static_cast<int>(N); p.K = static_cast<int>(K);
+  p.bias = bias; p.resid = resid; p.ld_resid = ld_resid; p.sum_out = sum_out; p.ld_sum = ld_sum;
+  p.out = out; p.ldo = ldo; p.out_f32 = (ln_epi && out_dtype == TK_F32) ? 1 : 0;
+  p.gamma = gamma; p.beta = beta; p.eps = eps;
+  p.row_len = row_len; p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : 1);
+  p.wait_limit_ns = g_wait_limit_ns.load();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (bn) {
+    case 64: return launch_gemm_epi<64>(epilogue, ma, mw, p, info, s);
+    case 128: return launch_gemm_epi<128>(epilogue, ma, mw, p, info, s);
+    case 256: return launch_gemm_epi<256>(epilogue, ma, mw, p, info, s);
+  }
+  return fail(TK_ERR_UNSUPPORTED, "tk_gemm: no kernel for tile width %d", bn);
+}
+
+int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, int64_t stride_h, int64_t stride_s,
+                void* out, int64_t ld_out, int64_t B, int64_t S, int64_t H, int64_t hd, float scale, int causal,
+                const int32_t* kv_len, void* stream) {
+  g_last_error.clear();
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(TK_ERR_INVALID, "tk_attn_fwd: null pointer");
+  if (B <= 0 || S <= 0 || H <= 0 || hd <= 0) return fail(TK_ERR_INVALID, "tk_attn_fwd: non-positive size");
+  if (!tk_attn_supported(hd))
+    return fail(TK_ERR_UNSUPPORTED, "tk_attn_fwd: head_dim %lld not in {32,64}", (long long)hd);
+  if (stride_b <= 0 || stride_h <= 0 || stride_s <= 0 || stride_b % 8 || stride_h % 8 || stride_s % 8 ||
+      !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
+    return fail(TK_ERR_INVALID, "tk_attn_fwd: q/k/v need 16-byte aligned bases and strides (multiples of 8 elements)");
+  if (ld_out < H * hd || ld_out % 8 || !aligned(out, 16))
+    return fail(TK_ERR_INVALID, "tk_attn_fwd: out needs 16-byte aligned rows and ld_out >= H*hd");
+  const int64_t q_tiles = (S + 127) / 128;
+  if (S > (1ll << 31) - 1 || B * H * q_tiles > (1ll << 31) - 1)
+    return fail(TK_ERR_UNSUPPORTED, "tk_attn_fwd: grid too large");
+  int dev;
+  DeviceInfo* info;
+  if (int st = current_device(&dev, &info)) return st;
+
+  CUtensorMap maps[3];
+  const void* bases[3] = {q, k, v};
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(stride_s) * 2, static_cast<cuuint64_t>(stride_h) * 2,
+                           static_cast<cuuint64_t>(stride_b) * 2};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(hd), 128, 1, 1};
+  for (int i = 0; i < 3; ++i)
+    if (int st = make_map_f16(&maps[i], bases[i], 4, dims, strides, box,
+                              hd == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
+      return st;
+  tk::attn::Params p;
+  p.out = static_cast<__half*>(out);
+  p.ld_out = ld_out;
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.H = static_cast<int>(H);
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal ? 1 : 0;
+  p.kv_len = kv_len;
+  p.wait_limit_ns = g_wait_limit_ns.load();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(B * H * q_tiles);
+  cudaError_t e;
+  if (hd == 64) {
+    auto kern = tk::attn::attn_fwd_kernel<64>;
+    {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      if (!info->attn_attr_set[1]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tk::attn::Cfg<64>::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn)");
+        info->attn_attr_set[1] = true;
+      }
+    }
+    kern<<<grid, tk::attn::kThreads, tk::attn::Cfg<64>::SMEM_BYTES, s>>>(maps[0], maps[1], maps[2], p);
+  } else {
+    auto kern = tk::attn::attn_fwd_kernel<32>;
+    {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      if (!info->attn_attr_set[0]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tk::attn::Cfg<32>::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn)");
+        info->attn_attr_set[0] = true;
+      }
+    }
+    kern<<<grid, tk::attn::kThreads, tk::attn::Cfg<32>::SMEM_BYTES, s>>>(maps[0], maps[1], maps[2], p);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tk_attn_fwd launch");
+  return TK_OK;
+}
+
+}  // extern "C"
+
+// ----------------------------------------------------------------------------
+// error word + self test
+// ----------------------------------------------------------------------------
+namespace {
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    tk::mbar_init(&bar, 1);
+    tk::fence_barrier_init();
+    // Nothing ever arrives on `bar`: the wait must give up after limit_ns.
+    if (!tk::mbar_wait(&bar, 0, nullptr, limit_ns)) tk::report_error(tk::kDevWaitTimeout, 0xFF01u);
+  }
+}
+}  // namespace
+
+extern "C" {
+
+int tk_selftest_wait_timeout(void* stream) {
+  g_last_error.clear();
+  int dev;
+  DeviceInfo* info;
+  if (int st = current_device(&dev, &info)) return st;
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(g_wait_limit_ns.load());
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  return TK_OK;
+}
+
+int tk_check_device_errors(void* stream) {
+  g_last_error.clear();
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  tk::ErrorWord w;
+  e = cudaMemcpyFromSymbol(&w, tk::g_error, sizeof(w));
+  if (e != cudaSuccess) return cuda_fail(e, "read error word");
+  if (w.code == tk::kDevOk) return TK_OK;
+  const tk::ErrorWord zero = {0, 0, 0, 0};
+  e = cudaMemcpyToSymbol(tk::g_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return cuda_fail(e, "clear error word");
+  if (w.code == tk::kDevWaitTimeout)
+    return fail(TK_ERR_TIMEOUT, "device wait timed out: site 0x%x, block %u, %u failure(s)", w.where, w.detail, w.count);
+  return fail(TK_ERR_DEVICE, "device error %u at site 0x%x, block %u, %u failure(s)", w.code, w.where, w.detail,
+              w.count);
+}
+
+}  // extern "C"

@@ -1,0 +1,403 @@
+// Persistent tcgen05 GEMM with fused epilogues:  out = epi(A[M,K] * W[N,K]^T + bias)
+//
+// Replaces the reference's cuBLAS F.linear calls and the elementwise work
+// that follows them (src/optimized.py:572 QKV, :627 O-proj, :632-636 FFN,
+// and the residual add of add_ln_fwd, src/fused_kernels.py:196-238):
+//   kBias         out16 = acc + b                              (QKV projection)
+//   kBiasGelu     out16 = gelu_erf(acc + b)                    (FFN in, fp32 erf)
+//   kBiasResid    s32   = resid + acc + b                      (O-proj / FFN out)
+//   kBiasResidLn  s32   = resid + acc + b;  h = LN(s) (fp32 statistics), N == BN
+//
+// A is the fp16 activation [M,K] (row-major = K-major), W the fp16
+// nn.Linear weight [N,K] as-is (also K-major). Both are staged by TMA into
+// 128B-swizzled shared-memory tiles of 64 K-columns; one elected thread
+// issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator. Two
+// accumulators (2*BN TMEM columns) let the epilogue of tile i overlap the
+// main loop of tile i+1.
+//
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 TMEM allocator + MMA
+// issuer, warps 2..9 epilogue. Epilogue warp w reads TMEM lanes
+// 32*(w%4)..+31 (the hardware lane quadrant of that warp) and columns
+// [half*BN/2, (half+1)*BN/2) with half = (w-2)/4.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "tk_ptx.cuh"
+
+namespace tk {
+namespace gemm {
+
+enum Epilogue : int { kBias = 0, kBiasGelu = 1, kBiasResid = 2, kBiasResidLn = 3 };
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // one 128-byte swizzle row of fp16
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+
+struct Params {
+  int M, N, K;
+  const float* bias;       // [N] fp32
+  const float* resid;      // [M, ld_resid] fp32 (resid epilogues)
+  int64_t ld_resid;
+  float* sum_out;          // [M, ld_sum] fp32 (resid epilogues)
+  int64_t ld_sum;
+  void* out;               // fp16 (kBias/kBiasGelu/LN) or fp32 (LN with out_f32)
+  int64_t ldo;
+  int out_f32;
+  const float* gamma;      // LN affine [N]
+  const float* beta;
+  float eps;
+  const int* row_len;      // optional per-sequence valid length: rows with
+  int seq_len;             //   (row % seq_len) >= row_len[row / seq_len] are zeroed
+  uint64_t wait_limit_ns;
+};
+
+template <int BN>
+struct Cfg {
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2 * 2 * kBM * 4 /*LN exchange*/;
+};
+
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
+
+// wait sites (error word "where" low byte)
+enum : unsigned { kSiteEmpty = 1, kSiteFull = 2, kSiteAccEmpty = 3, kSiteAccFull = 4, kSiteDrain = 5, kSiteLn = 6 };
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, Params p) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ __align__(8) uint64_t ln_bar[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* ln_part = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);  // [2 halves][2 stats][128 rows]
+
+  const int warp = warp_id_uniform();
+  const uint32_t lane = lane_id();
+  const int m_tiles = (p.M + kBM - 1) / kBM;
+  const int n_tiles = (p.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+  const unsigned kid = (EPI + 1) * 16 + (BN >> 6);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kEpiWarps);
+    }
+    mbar_init(&drain_bar, 1);
+    mbar_init(&ln_bar[0], kEpiWarps * 32);
+    mbar_init(&ln_bar[1], kEpiWarps * 32);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&map_a);
+    prefetch_tensormap(&map_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * kBM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteEmpty);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+          tma_load_2d(sa, &map_a, &full_bar[stage], kb * kBK, m0);
+          tma_load_2d(sb, &map_w, &full_bar[stage], kb * kBK, n0);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already in flight land before the CTA can exit:
+        // drain every stage that the MMA side has not consumed (bounded).
+        for (int s = 0; s < C::STAGES; ++s)
+          mbar_wait(&full_bar[s], phase ^ (s < stage ? 0u : 1u), nullptr, kDrainLimitNs);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
+          report_error(kDevWaitTimeout, kid * 256 + kSiteAccEmpty);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteFull);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
+            const uint64_t db = smem_desc(b_addr + kk * 32, 16, 1024, kLayoutSW128);
+            mma_f16_ss(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(&acc_full[acc]);
+      }
+      // All MMAs this thread issued are complete before TMEM is released.
+      mma_commit(&drain_bar);
+      if (!mbar_wait(&drain_bar, 0, nullptr, p.wait_limit_ns) && ok)
+        report_error(kDevWaitTimeout, kid * 256 + kSiteDrain);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue ----------------
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int HALF_N = BN / 2;
+    const int row_in_tile = quad * 32 + static_cast<int>(lane);
+    int it = 0;
+    uint32_t ln_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, &abort_flag, p.wait_limit_ns)) {
+        report_error(kDevWaitTimeout, kid * 256 + kSiteAccFull);
+        abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (tile / n_tiles) * kBM;
+      const int n0 = (tile % n_tiles) * BN;
+      const int row = m0 + row_in_tile;
+      const bool row_ok = row < p.M;
+      bool row_zero = false;
+      if (p.row_len != nullptr && row_ok) row_zero = (row % p.seq_len) >= p.row_len[row / p.seq_len];
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + half * HALF_N;
+
+      if constexpr (EPI == kBias || EPI == kBiasGelu) {
+#pragma unroll 1
+        for (int c = 0; c < HALF_N; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c, r);
+          tmem_ld_wait();
+          const int col0 = n0 + half * HALF_N + c;
+          if (row_ok && col0 < p.N) {
+            __half* dst = static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
+            const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              const float4 ba = __ldg(b4 + j / 4), bb = __ldg(b4 + j / 4 + 1);
+              float v[8] = {__uint_as_float(r[j + 0]) + ba.x, __uint_as_float(r[j + 1]) + ba.y,
+                            __uint_as_float(r[j + 2]) + ba.z, __uint_as_float(r[j + 3]) + ba.w,
+                            __uint_as_float(r[j + 4]) + bb.x, __uint_as_float(r[j + 5]) + bb.y,
+                            __uint_as_float(r[j + 6]) + bb.z, __uint_as_float(r[j + 7]) + bb.w};
+              if constexpr (EPI == kBiasGelu) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = gelu_erf(v[k]);
+              }
+              if (row_zero) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = 0.f;
+              }
+              uint4 o;
+              o.x = pack_half2(v[0], v[1]);
+              o.y = pack_half2(v[2], v[3]);
+              o.z = pack_half2(v[4], v[5]);
+              o.w = pack_half2(v[6], v[7]);
+              *reinterpret_cast<uint4*>(dst + j) = o;
+            }
+          }
+        }
+      } else {
+        // s = resid + acc + bias, written to sum_out (fp32). For kBiasResidLn
+        // s is also written back into TMEM for the two statistic passes.
+        float part_sum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < HALF_N; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c, r);
+          tmem_ld_wait();
+          const int col0 = n0 + half * HALF_N + c;
+          if (row_ok && col0 < p.N) {
+            const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+            const float4* r4 = reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(row) * p.ld_resid + col0);
+            float4* s4 = reinterpret_cast<float4*>(p.sum_out + static_cast<int64_t>(row) * p.ld_sum + col0);
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 bb = __ldg(b4 + j / 4);
+              const float4 rr = r4[j / 4];  // plain load: resid may alias sum_out
+              float4 s;
+              s.x = rr.x + (__uint_as_float(r[j + 0]) + bb.x);
+              s.y = rr.y + (__uint_as_float(r[j + 1]) + bb.y);
+              s.z = rr.z + (__uint_as_float(r[j + 2]) + bb.z);
+              s.w = rr.w + (__uint_as_float(r[j + 3]) + bb.w);
+              if (row_zero) s = make_float4(0.f, 0.f, 0.f, 0.f);
+              s4[j / 4] = s;
+              r[j + 0] = __float_as_uint(s.x);
+              r[j + 1] = __float_as_uint(s.y);
+              r[j + 2] = __float_as_uint(s.z);
+              r[j + 3] = __float_as_uint(s.w);
+              part_sum += (s.x + s.y) + (s.z + s.w);
+            }
+          }
+          if constexpr (EPI == kBiasResidLn) {
+            uint32_t lo[16], hi[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              lo[k] = r[k];
+              hi[k] = r[16 + k];
+            }
+            tmem_st16(t_row + c, lo);
+            tmem_st16(t_row + c + 16, hi);
+          }
+        }
+        if constexpr (EPI == kBiasResidLn) {
+          tmem_st_wait();
+          // Row statistics over the full row (N == BN): the two epilogue
+          // warps of a lane quadrant each hold half the row.
+          const float inv_n = 1.f / static_cast<float>(p.N);
+          ln_part[(half * 2 + 0) * kBM + row_in_tile] = part_sum;
+          mbar_arrive(&ln_bar[0]);
+          if (!mbar_wait(&ln_bar[0], ln_phase, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteLn);
+            abort_flag = 1;
+            break;
+          }
+          const float mean = (ln_part[0 * kBM + row_in_tile] + ln_part[2 * kBM + row_in_tile]) * inv_n;
+          float part_sq = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < HALF_N; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float t = __uint_as_float(r[j]) - mean;
+              part_sq += t * t;
+            }
+          }
+          ln_part[(half * 2 + 1) * kBM + row_in_tile] = part_sq;
+          mbar_arrive(&ln_bar[1]);
+          if (!mbar_wait(&ln_bar[1], ln_phase, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteLn);
+            abort_flag = 1;
+            break;
+          }
+          ln_phase ^= 1u;
+          const float var = (ln_part[1 * kBM + row_in_tile] + ln_part[3 * kBM + row_in_tile]) * inv_n;
+          const float rstd = rsqrtf(var + p.eps);
+#pragma unroll 1
+          for (int c = 0; c < HALF_N; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+            tmem_ld_wait();
+            const int col0 = n0 + half * HALF_N + c;
+            if (row_ok) {
+              const float4* g4 = reinterpret_cast<const float4*>(p.gamma + col0);
+              const float4* be4 = reinterpret_cast<const float4*>(p.beta + col0);
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 g = __ldg(g4 + j / 4), be = __ldg(be4 + j / 4);
+                v[j + 0] = (__uint_as_float(r[j + 0]) - mean) * rstd * g.x + be.x;
+                v[j + 1] = (__uint_as_float(r[j + 1]) - mean) * rstd * g.y + be.y;
+                v[j + 2] = (__uint_as_float(r[j + 2]) - mean) * rstd * g.z + be.z;
+                v[j + 3] = (__uint_as_float(r[j + 3]) - mean) * rstd * g.w + be.w;
+              }
+              if (row_zero) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = 0.f;
+              }
+              if (p.out_f32) {
+                float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) o4[j / 4] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              } else {
+                uint4* o4 = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0);
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                  uint4 o;
+                  o.x = pack_half2(v[j + 0], v[j + 1]);
+                  o.y = pack_half2(v[j + 2], v[j + 3]);
+                  o.z = pack_half2(v[j + 4], v[j + 5]);
+                  o.w = pack_half2(v[j + 6], v[j + 7]);
+                  o4[j / 8] = o;
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+}  // namespace gemm
+}  // namespace tk

@@ -1,0 +1,308 @@
+"""Drop-in ``UserOptimizedTransformer`` running on the B200 kernels.
+
+Mirrors the reference's ``src/optimized.py`` surface: ``OptimizerSettings``,
+``configure(**kw)`` / ``active_settings()`` (module-global settings, because
+the harness constructs ``UserOptimizedTransformer(config)`` with no other
+argument, :145-153) and ``OptimizedTransformer(config, settings=None)``
+with the harness's ``forward(x, valid_token_mask=None)``.
+
+The module tree is the harness's ``BaselineTransformer`` tree
+(``src/torch_transformer_benchmark.py:125-160``: ``layers.{i}.norm1``,
+``layers.{i}.attention.{q,k,v,out}_proj``, ``layers.{i}.norm2``,
+``layers.{i}.ffn_in``, ``layers.{i}.ffn_out``, ``final_norm``), so the
+harness's strict ``load_state_dict`` copy works unchanged. Derived tensors
+(fp16 weights, the concatenated QKV weight) are plain attributes, never
+parameters or buffers, and are dropped on ``_apply`` (``.to()``), as the
+reference does (:224-244).
+
+Forward, per layer (``T = B*S`` token rows, fp32 residual stream):
+
+  h    = LN1(x)                                   tk_layernorm        (layer 0 only)
+  qkv  = h Wqkv^T + bqkv                          tk_gemm  BIAS       fp16 [T, 3d]
+  ctx  = attention(q, k, v views of qkv)          tk_attn_fwd         fp16 [T, d]
+  x, h = x + ctx Wo^T + bo,  LN2(.)               tk_gemm  RESID_LN   (d in {64,128,256})
+                                                  or RESID + tk_layernorm
+  u    = gelu(h W1^T + b1)                        tk_gemm  GELU       fp16 [T, ffn]
+  x, h = x + u W2^T + b2,  next LN1 / final LN    tk_gemm  RESID_LN  or RESID + tk_layernorm
+
+The final LayerNorm writes the fp32 output directly. There is no CPU,
+SDPA, cuBLAS or Triton path: anything the kernels cannot do raises.
+"""
+
+from __future__ import annotations
+
+import weakref
+from dataclasses import dataclass, replace
+from typing import List, Optional
+
+import torch
+import torch.nn as nn
+
+import _tklib as tk
+import kernels
+import linear as tk_linear
+
+__all__ = ["OptimizerSettings", "OptimizedTransformer", "TransformerConfig", "configure", "active_settings"]
+
+
+@dataclass(frozen=True)
+class TransformerConfig:
+    """Same fields as the harness's ``TransformerConfig``
+    (``src/torch_transformer_benchmark.py:29-56``); any object with these
+    attributes is accepted by ``OptimizedTransformer``."""
+
+    batch_size: int
+    seq_len: int
+    d_model: int
+    num_heads: int
+    ffn_dim: int
+    num_layers: int
+    causal: bool
+
+
+@dataclass(frozen=True)
+class OptimizerSettings:
+    """Knobs of the B200 forward. None of them selects another backend."""
+
+    # Fuse residual add + LayerNorm into the O-projection / FFN-out GEMM
+    # epilogue when d_model fits one tile row (64, 128 or 256); wider models
+    # use the GEMM residual epilogue followed by tk_layernorm.
+    fused_ln_epilogue: bool = True
+    # Skip the one device->host sync that checks whether the mask is all-True.
+    assume_dense_mask: bool = False
+    # Synchronise after every forward and raise if a kernel's bounded
+    # device-side wait gave up (debugging aid; costs a sync per call).
+    check_device_errors: bool = False
+
+
+_ACTIVE = OptimizerSettings()
+
+
+def configure(**kwargs) -> OptimizerSettings:
+    """Set the settings used by ``OptimizedTransformer(config)``."""
+    global _ACTIVE
+    _ACTIVE = replace(_ACTIVE, **kwargs)
+    return _ACTIVE
+
+
+def active_settings() -> OptimizerSettings:
+    return _ACTIVE
+
+
+def _outside_compile(fn):
+    disable = getattr(getattr(torch, "compiler", None), "disable", None)
+    return disable(fn) if disable is not None else fn
+
+
+class _Attention(nn.Module):
+    def __init__(self, d_model: int, num_heads: int) -> None:
+        super().__init__()
+        if d_model % num_heads != 0:
+            raise ValueError("d_model must be divisible by num_heads")
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.q_proj = nn.Linear(d_model, d_model, bias=True)
+        self.k_proj = nn.Linear(d_model, d_model, bias=True)
+        self.v_proj = nn.Linear(d_model, d_model, bias=True)
+        self.out_proj = nn.Linear(d_model, d_model, bias=True)
+
+
+class _Block(nn.Module):
+    def __init__(self, d_model: int, num_heads: int, ffn_dim: int) -> None:
+        super().__init__()
+        self.norm1 = nn.LayerNorm(d_model)
+        self.attention = _Attention(d_model, num_heads)
+        self.norm2 = nn.LayerNorm(d_model)
+        self.ffn_in = nn.Linear(d_model, ffn_dim)
+        self.ffn_out = nn.Linear(ffn_dim, d_model)
+
+
+@dataclass
+class _LayerWeights:
+    norm1_w: torch.Tensor
+    norm1_b: torch.Tensor
+    norm1_eps: float
+    qkv_w: torch.Tensor     # fp16 [3d, d] = [Wq; Wk; Wv]
+    qkv_b: torch.Tensor     # fp32 [3d]
+    out_w: torch.Tensor     # fp16 [d, d]
+    out_b: torch.Tensor
+    norm2_w: torch.Tensor
+    norm2_b: torch.Tensor
+    norm2_eps: float
+    ffn_in_w: torch.Tensor  # fp16 [ffn, d]
+    ffn_in_b: torch.Tensor
+    ffn_out_w: torch.Tensor  # fp16 [d, ffn]
+    ffn_out_b: torch.Tensor
+
+
+class OptimizedTransformer(nn.Module):
+    """B200 drop-in for the harness's ``UserOptimizedTransformer``."""
+
+    def __init__(self, config, settings: Optional[OptimizerSettings] = None) -> None:
+        super().__init__()
+        self.config = config
+        self.settings = settings if settings is not None else _ACTIVE
+        self.layers = nn.ModuleList(
+            [_Block(config.d_model, config.num_heads, config.ffn_dim) for _ in range(config.num_layers)]
+        )
+        self.final_norm = nn.LayerNorm(config.d_model)
+        self.d_model = config.d_model
+        self.num_heads = config.num_heads
+        self.head_dim = config.d_model // config.num_heads
+        self.attn_scale = self.head_dim ** -0.5
+        self._weight_cache: Optional[List[_LayerWeights]] = None
+        self._weight_cache_key: Optional[tuple] = None
+        self._mask_ref: Optional[weakref.ReferenceType] = None
+        self._mask_lengths: Optional[torch.Tensor] = None  # None = dense
+        # Optional launch trace: a list that receives (name, start, end)
+        # CUDA events around every kernel launch of the next forwards.
+        self.launch_trace: Optional[list] = None
+
+    # -- caches ---------------------------------------------------------------
+    def _apply(self, *args, **kwargs):
+        result = super()._apply(*args, **kwargs)
+        self._weight_cache = None
+        self._weight_cache_key = None
+        return result
+
+    @_outside_compile
+    def _weights(self) -> List[_LayerWeights]:
+        ref = self.layers[0].attention.q_proj.weight
+        key = (ref.device, ref.dtype, ref.data_ptr())
+        if self._weight_cache is not None and self._weight_cache_key == key:
+            return self._weight_cache
+        built = []
+        with torch.no_grad():
+            f16 = lambda t: t.detach().to(torch.float16).contiguous()  # noqa: E731
+            f32 = lambda t: t.detach().to(torch.float32).contiguous()  # noqa: E731
+            for layer in self.layers:
+                a = layer.attention
+                built.append(
+                    _LayerWeights(
+                        norm1_w=f32(layer.norm1.weight), norm1_b=f32(layer.norm1.bias), norm1_eps=layer.norm1.eps,
+                        qkv_w=f16(torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0)),
+                        qkv_b=f32(torch.cat([a.q_proj.bias, a.k_proj.bias, a.v_proj.bias], 0)),
+                        out_w=f16(a.out_proj.weight), out_b=f32(a.out_proj.bias),
+                        norm2_w=f32(layer.norm2.weight), norm2_b=f32(layer.norm2.bias), norm2_eps=layer.norm2.eps,
+                        ffn_in_w=f16(layer.ffn_in.weight), ffn_in_b=f32(layer.ffn_in.bias),
+                        ffn_out_w=f16(layer.ffn_out.weight), ffn_out_b=f32(layer.ffn_out.bias),
+                    )
+                )
+        self._final = (f32(self.final_norm.weight), f32(self.final_norm.bias), self.final_norm.eps)
+        self._weight_cache, self._weight_cache_key = built, key
+        return built
+
+    @_outside_compile
+    def _prefix_lengths(self, mask: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+        """``None`` for an all-True (or absent) mask, else the int32 per-row
+        prefix lengths. One device->host sync per distinct mask object
+        (weakref memo, like the reference's ``_mask_is_dense``, :362-389).
+        Masks that are not per-row prefixes -- the only kind the harness's
+        ``generate_random_case`` makes (:261-271) -- raise."""
+        if mask is None or self.settings.assume_dense_mask:
+            return None
+        if self._mask_ref is not None and self._mask_ref() is mask:
+            return self._mask_lengths
+        m = mask.to(torch.bool)
+        lengths = m.sum(dim=-1, dtype=torch.int32)
+        if bool(m.all()):
+            result = None
+        else:
+            prefix = torch.arange(m.shape[-1], device=m.device)[None, :] < lengths[:, None]
+            if not bool((prefix == m).all()):
+                raise tk.TKError("forward", -2, "valid_token_mask must be a per-row prefix (True then False)")
+            result = lengths.contiguous()
+        self._mask_ref = weakref.ref(mask)
+        self._mask_lengths = result
+        return result
+
+    # -- forward --------------------------------------------------------------
+    def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if not x.is_cuda:
+            raise tk.TKError("forward", -1, "OptimizedTransformer runs on the B200 kernels only; x must be a CUDA tensor")
+        if x.dim() != 3 or x.shape[-1] != self.d_model:
+            raise ValueError(f"expected x of shape [B, S, {self.d_model}], got {tuple(x.shape)}")
+        lengths = self._prefix_lengths(valid_token_mask)
+        out = self._run(x, lengths)
+        if self.settings.check_device_errors:
+            tk.check_device_errors(x.device)
+        return out if out.dtype == x.dtype else out.to(x.dtype)
+
+    def _run(self, x: torch.Tensor, lengths: Optional[torch.Tensor]) -> torch.Tensor:
+        B, S, d = x.shape
+        T = B * S
+        dev = x.device
+        weights = self._weights()
+        ffn = weights[0].ffn_in_w.shape[0]
+        hd = self.head_dim
+        fused = self.settings.fused_ln_epilogue and tk_linear.fused_ln_supported(d)
+        xin = x.reshape(T, d)
+        if xin.dtype != torch.float32 or xin.stride(-1) != 1 or xin.stride(0) != d:
+            xin = xin.to(torch.float32).contiguous()
+        seq = S if lengths is not None else 0
+
+        res = torch.empty((T, d), dtype=torch.float32, device=dev)
+        h = torch.empty((T, d), dtype=torch.float16, device=dev)
+        qkv = torch.empty((T, 3 * d), dtype=torch.float16, device=dev)
+        ctx = torch.empty((B, S, d), dtype=torch.float16, device=dev)
+        u = torch.empty((T, ffn), dtype=torch.float16, device=dev)
+        out = torch.empty((T, d), dtype=torch.float32, device=dev)
+        stream = tk.stream_handle(dev)
+
+        def layer_norm(src, w, b, eps, dst, zero_padded):
+            tk.call(
+                "tk_layernorm",
+                src.data_ptr(), tk.TK_F32, src.stride(0), None, 0, 0, None, 0,
+                w.data_ptr(), b.data_ptr(), float(eps),
+                dst.data_ptr(), tk.dtype_code(dst.dtype), dst.stride(0),
+                tk.ptr(lengths) if zero_padded else None, seq if zero_padded else 0,
+                T, d, stream,
+            )
+
+        trace = self.launch_trace
+
+        def run(name, fn, *args, **kwargs):
+            if trace is None:
+                return fn(*args, **kwargs)
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            result = fn(*args, **kwargs)
+            end.record()
+            trace.append((name, start, end))
+            return result
+
+        lin = tk_linear.linear
+        with torch.cuda.device(dev):
+            w0 = weights[0]
+            run("ln", layer_norm, xin, w0.norm1_w, w0.norm1_b, w0.norm1_eps, h, False)
+            resid = xin
+            # q/k/v as [B, H, S, hd] views of the fused projection
+            qkv4 = qkv.view(B, S, 3, self.num_heads, hd)
+            q, k, v = qkv4.permute(2, 0, 3, 1, 4).unbind(0)
+            last = len(weights) - 1
+            for i, w in enumerate(weights):
+                run("gemm_qkv", lin, h, w.qkv_w, w.qkv_b, "bias", out=qkv)
+                run("attn", kernels.flash_attention, q, k, v, self.attn_scale, self.config.causal,
+                    kv_len=lengths, out=ctx)
+                ctx2 = ctx.view(T, d)
+                if fused:
+                    run("gemm_o_ln", lin, ctx2, w.out_w, w.out_b, "resid_ln", resid=resid, sum_out=res,
+                        ln_weight=w.norm2_w, ln_bias=w.norm2_b, eps=w.norm2_eps, out=h)
+                else:
+                    run("gemm_o", lin, ctx2, w.out_w, w.out_b, "resid", resid=resid, sum_out=res)
+                    run("ln", layer_norm, res, w.norm2_w, w.norm2_b, w.norm2_eps, h, False)
+                resid = res
+                run("gemm_ffn_in", lin, h, w.ffn_in_w, w.ffn_in_b, "gelu", out=u)
+                if i < last:
+                    nw, nb, neps, dst = weights[i + 1].norm1_w, weights[i + 1].norm1_b, weights[i + 1].norm1_eps, h
+                else:
+                    nw, nb, neps = self._final
+                    dst = out
+                if fused:
+                    run("gemm_ffn_out_ln", lin, u, w.ffn_out_w, w.ffn_out_b, "resid_ln", resid=res, sum_out=res,
+                        ln_weight=nw, ln_bias=nb, eps=neps, out=dst, row_len=lengths, seq_len=seq)
+                else:
+                    run("gemm_ffn_out", lin, u, w.ffn_out_w, w.ffn_out_b, "resid", resid=res, sum_out=res,
+                        row_len=lengths, seq_len=seq)
+                    run("ln", layer_norm, res, nw, nb, neps, dst, lengths is not None)
+        return out.view(B, S, d)
