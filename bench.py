@@ -83,11 +83,17 @@ class Clocks:
         self.proc = None
 
     def __enter__(self):
+        import tempfile
+
+        self.path = tempfile.mktemp(prefix="tk_clocks_", suffix=".csv")
         try:
+            # -f writes each sample straight to the file (a pipe would be
+            # block-buffered and lost when the sampler is stopped).
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.index)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-i", str(self.index), "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.5)  # first sample lands before the timed region
         except OSError:
             self.proc = None
         return self
@@ -95,13 +101,18 @@ class Clocks:
     def __exit__(self, *exc):
         self.lines = []
         if self.proc is not None:
+            time.sleep(0.3)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+                self.proc.wait()
+            try:
+                self.lines = [ln for ln in pathlib.Path(self.path).read_text().splitlines() if ln.strip()]
+                os.unlink(self.path)
+            except OSError:
+                self.lines = []
 
     def summary(self):
         sms, maxes, reasons = [], [], set()
@@ -181,6 +192,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="C3", choices=sorted(CONFIGS))
+    ap.add_argument("--batch", type=int, default=0, help="override the config's batch (small profiling cases)")
     ap.add_argument("--impl", default="tk", choices=["tk", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -192,6 +204,8 @@ def main() -> int:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     cfg_tuple = CONFIGS[args.config]
+    if args.batch > 0:
+        cfg_tuple = (args.batch,) + cfg_tuple[1:]
     B, S, d, H, ffn, L, causal = cfg_tuple
 
     if args.impl == "reference":

@@ -60,7 +60,8 @@ int make_map_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t*
                  const cuuint32_t* box, CUtensorMapSwizzle swz) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(TK_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable from the driver");
-  cuuint32_t estr[3] = {1, 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  if (rank < 1 || rank > 5) return fail(TK_ERR_INVALID, "tensor map rank %d", rank);
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -322,11 +323,18 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
 
   CUtensorMap maps[3];
   const void* bases[3] = {q, k, v};
-  cuuint64_t dims[4] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(H),
-                        static_cast<cuuint64_t>(B)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(stride_s) * 2, static_cast<cuuint64_t>(stride_h) * 2,
+  // Dimensions in increasing stride order (the encoder rejects others).
+  const bool heads_inner = stride_h < stride_s;
+  const int64_t mid_dim[2] = {heads_inner ? H : S, heads_inner ? S : H};
+  const int64_t mid_stride[2] = {heads_inner ? stride_h : stride_s, heads_inner ? stride_s : stride_h};
+  if (mid_stride[0] < hd || mid_stride[1] < mid_stride[0] || stride_b < mid_stride[1])
+    return fail(TK_ERR_UNSUPPORTED, "tk_attn_fwd: strides (b=%lld, h=%lld, s=%lld) overlap", (long long)stride_b,
+                (long long)stride_h, (long long)stride_s);
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(mid_dim[0]),
+                        static_cast<cuuint64_t>(mid_dim[1]), static_cast<cuuint64_t>(B)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(mid_stride[0]) * 2, static_cast<cuuint64_t>(mid_stride[1]) * 2,
                            static_cast<cuuint64_t>(stride_b) * 2};
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(hd), 128, 1, 1};
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(hd), heads_inner ? 1u : 128u, heads_inner ? 128u : 1u, 1};
   for (int i = 0; i < 3; ++i)
     if (int st = make_map_f16(&maps[i], bases[i], 4, dims, strides, box,
                               hd == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
@@ -340,6 +348,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
   p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal ? 1 : 0;
   p.kv_len = kv_len;
+  p.heads_inner = heads_inner ? 1 : 0;
   p.wait_limit_ns = g_wait_limit_ns.load();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned grid = static_cast<unsigned>(B * H * q_tiles);

@@ -11,8 +11,11 @@
 // Inputs: q, k, v fp16, logically [B, H, S, hd] with any strides whose last
 // dimension is contiguous -- in the model they are views into the QKV GEMM's
 // [B, S, 3*d] output, so no head-split copy is made. One 4-D tensor map per
-// operand (dims {hd, S, H, B}) lets TMA fetch the tile of one (b, h)
-// directly, zero-filling rows past S.
+// operand lets TMA fetch the tile of one (b, h) directly, zero-filling rows
+// past S. The map lists dimensions in increasing stride order, as the
+// tensor-map encoder requires: {hd, H, S, B} for views into the fused
+// projection (head stride hd < row stride 3d), {hd, S, H, B} for [B,H,S,hd]
+// contiguous tensors.
 //
 // Per CTA: one (b, h, 128-query tile). Warp 0 issues TMA, warp 1 owns TMEM
 // and issues tcgen05.mma, warps 2..5 (one TMEM lane quadrant each, one query
@@ -54,8 +57,18 @@ struct Params {
   float scale_log2;     // hd**-0.5 * log2(e)
   int causal;
   const int* kv_len;    // optional [B]: keys >= kv_len[b] are masked
+  int heads_inner;      // tensor-map dim order {hd, H, S, B} (1) or {hd, S, H, B} (0)
   uint64_t wait_limit_ns;
 };
+
+// TMA coordinates of the tile of (b, h) starting at sequence row `row`.
+__device__ __forceinline__ void load_tile(void* dst, const CUtensorMap* map, uint64_t* bar, const Params& p, int row,
+                                          int h, int b) {
+  if (p.heads_inner)
+    tma_load_4d(dst, map, bar, 0, h, row, b);
+  else
+    tma_load_4d(dst, map, bar, 0, row, h, b);
+}
 
 template <int HD>
 struct Cfg {
@@ -131,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
       mbar_arrive_expect_tx(&q_full, C::TILE_BYTES);
-      tma_load_4d(sQ, &map_q, &q_full, 0, qt * kBM, h, b);
+      load_tile(sQ, &map_q, &q_full, p, qt * kBM, h, b);
       bool ok = true;
       int j = 0;
       for (; j < n_kv; ++j) {
@@ -144,8 +157,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           break;
         }
         mbar_arrive_expect_tx(&kv_full[s], 2 * C::TILE_BYTES);
-        tma_load_4d(sK + s * C::TILE_BYTES, &map_k, &kv_full[s], 0, j * kBN, h, b);
-        tma_load_4d(sV + s * C::TILE_BYTES, &map_v, &kv_full[s], 0, j * kBN, h, b);
+        load_tile(sK + s * C::TILE_BYTES, &map_k, &kv_full[s], p, j * kBN, h, b);
+        load_tile(sV + s * C::TILE_BYTES, &map_v, &kv_full[s], p, j * kBN, h, b);
       }
       if (!ok) {
         mbar_wait(&q_full, 0, nullptr, kDrainLimitNs);
