@@ -221,11 +221,15 @@ def main() -> int:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     import _tklib as tk
+    import cuda_graphs
     import optimized
 
     ocfg = optimized.TransformerConfig(B, S, d, H, ffn, L, causal)
     torch.manual_seed(0)
-    model = optimized.OptimizedTransformer(ocfg).to(dev).eval()
+    # The public graph-replaying drop-in (the reference's --cuda-graphs
+    # path); its eager superclass forward is used for the per-kernel trace.
+    model = cuda_graphs.GraphedTransformer(ocfg).to(dev).eval()
+    eager_forward = optimized.OptimizedTransformer.forward
     gen = torch.Generator().manual_seed(1234 + 100000)
     x_host = torch.randn(B, S, d, generator=gen).pin_memory()
     mask_host = torch.ones(B, S, dtype=torch.bool).pin_memory()
@@ -246,7 +250,9 @@ def main() -> int:
         return float(t.item())
 
     with torch.inference_mode():
-        # ---- device-resident timing ----
+        # ---- graph capture (untimed), then device-resident timing ----
+        for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 1):
+            model(x, mask)
         for _ in range(args.warmup):
             model(x, mask)
         tk.check_device_errors(dev)
@@ -268,7 +274,7 @@ def main() -> int:
         trace = []
         model.launch_trace = trace
         for _ in range(args.steps):
-            model(x, mask)
+            eager_forward(model, x, mask)
         torch.cuda.synchronize(dev)
         model.launch_trace = None
         per = {}

@@ -117,3 +117,25 @@ def test_batch_rows_are_independent(cuda_device):
         full = model(x.cuda(), mask.cuda())
         part = model(x[2:5].cuda(), mask[2:5].cuda())
     torch.testing.assert_close(full[2:5], part, atol=0, rtol=0)
+
+
+def test_cuda_graph_replay_matches_eager(cuda_device):
+    import cuda_graphs
+
+    cfg = StackConfig(8, 128, 128, 4, 128, 2, True)
+    params = init_params(cfg, seed=0)
+    graphed = cuda_graphs.GraphedTransformer(cfg)
+    graphed.load_state_dict(params, strict=True)
+    graphed = graphed.cuda().eval()
+    x, mask = generate_random_case(cfg, 7)
+    x2, _ = generate_random_case(cfg, 8)
+    xd, md, x2d = x.cuda(), mask.cuda(), x2.cuda()
+    with torch.inference_mode():
+        eager = optimized.OptimizedTransformer.forward(graphed, xd, md).clone()
+        outs = [graphed(xd, md).clone() for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 3)]
+        assert graphed._graph_states and next(iter(graphed._graph_states.values())).graph is not None
+        other = graphed(x2d, md).clone()  # different tensor: copied into the captured input
+        eager2 = optimized.OptimizedTransformer.forward(graphed, x2d, md)
+    for o in outs:
+        torch.testing.assert_close(o, eager, atol=0, rtol=0)
+    torch.testing.assert_close(other, eager2, atol=0, rtol=0)

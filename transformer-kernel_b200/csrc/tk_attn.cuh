@@ -242,17 +242,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (p.causal) lim = min(lim, q_idx - k0 + 1);
       lim = max(0, min(kBN, lim));
 
-      // pass A: row max over valid keys
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(t_lane + c, v);
-        tmem_ld_wait();
+      // The whole 128-column score row in registers: one TMEM round trip.
+      uint32_t sv[4][32];
 #pragma unroll
-        for (int t = 0; t < 32; ++t)
-          if (c + t < lim) mx = fmaxf(mx, __uint_as_float(v[t]));
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_lane + c * 32, sv[c]);
+      tmem_ld_wait();
+      // Masking is only needed on the causal diagonal tile and the tile
+      // holding the kv bound; `full` is warp-uniform elsewhere.
+      const bool full = lim >= kBN;
+      // row max with four independent chains
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (full) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; ++t) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; ++t)
+            if (c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
       }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       float m_use = m;
       float alpha = 1.f;
       if (mx > m) {
@@ -262,23 +274,26 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * p.scale_log2;
-      // pass B: P = 2^(s*c - m*c), packed fp16 over S columns [0, 64)
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(t_lane + c, v);
-        tmem_ld_wait();
+      // P = 2^(s*c - m*c), packed fp16 pairs over S columns [0, 64); the
+      // columns written for chunk c were all read into registers above.
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          const float p0 = (c + t < lim) ? ex2_approx(fmaf(__uint_as_float(v[t]), p.scale_log2, neg_mc)) : 0.f;
-          const float p1 = (c + t + 1 < lim) ? ex2_approx(fmaf(__uint_as_float(v[t + 1]), p.scale_log2, neg_mc)) : 0.f;
-          rs += p0 + p1;
+          float p0 = ex2_approx(fmaf(__uint_as_float(sv[c][t]), p.scale_log2, neg_mc));
+          float p1 = ex2_approx(fmaf(__uint_as_float(sv[c][t + 1]), p.scale_log2, neg_mc));
+          if (!full) {
+            p0 = (c * 32 + t < lim) ? p0 : 0.f;
+            p1 = (c * 32 + t + 1 < lim) ? p1 : 0.f;
+          }
+          rs4[(t >> 1) & 3] += p0 + p1;
           pk[t / 2] = pack_half2(p0, p1);
         }
-        tmem_st16(t_lane + c / 2, pk);
+        tmem_st16(t_lane + c * 16, pk);
       }
+      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       // O rescale: S_j's completion implies PV_{j-1} (issued before it) is done.
       const bool need = (j > 0) && (alpha != 1.f);
       if (__any_sync(0xffffffffu, need)) {

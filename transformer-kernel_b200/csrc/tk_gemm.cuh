@@ -55,15 +55,22 @@ struct Params {
   uint64_t wait_limit_ns;
 };
 
+// Epilogue staging: each epilogue warp transposes 32 rows x 16 fp32 columns
+// through 2 KB of shared memory so that global loads/stores run along rows.
+constexpr int kStageCols = 16;
+constexpr int kStageBytesPerWarp = 32 * kStageCols * 4;
+
 template <int BN>
 struct Cfg {
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (196 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 2 * 2 * kBM * 4 /*LN exchange*/;
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;                    // epilogue staging
+  static constexpr int LN_OFFSET = EPI_OFFSET + kEpiWarps * kStageBytesPerWarp;  // LN row partials
+  static constexpr int SMEM_BYTES = LN_OFFSET + 2 * 2 * kBM * 4 + 1024 /*align*/;
 };
 
 __device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
@@ -86,7 +93,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ volatile int abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* ln_part = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);  // [2 halves][2 stats][128 rows]
+  float* ln_part = reinterpret_cast<float*>(smem + C::LN_OFFSET);  // [2 halves][2 stats][128 rows]
 
   const int warp = warp_id_uniform();
   const uint32_t lane = lane_id();
@@ -233,40 +240,65 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.row_len != nullptr && row_ok) row_zero = (row % p.seq_len) >= p.row_len[row / p.seq_len];
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + half * HALF_N;
 
-      if constexpr (EPI == kBias || EPI == kBiasGelu) {
+      if constexpr (EPI != kBiasResidLn) {
+        // Thread-per-row TMEM chunk -> swizzled staging -> row-contiguous
+        // global traffic (lane -> row it*8 + lane/4, float4 column lane%4).
+        float* stage = reinterpret_cast<float*>(smem + C::EPI_OFFSET) + (warp - 2) * (32 * kStageCols);
+        float4* my_row = reinterpret_cast<float4*>(stage + lane * kStageCols);
+        const int sub_row = static_cast<int>(lane >> 2), sub_c4 = static_cast<int>(lane & 3);
 #pragma unroll 1
-        for (int c = 0; c < HALF_N; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c, r);
+        for (int c = 0; c < HALF_N; c += kStageCols) {
+          uint32_t r[16];
+          tmem_ld16(t_row + c, r);
           tmem_ld_wait();
           const int col0 = n0 + half * HALF_N + c;
-          if (row_ok && col0 < p.N) {
-            __half* dst = static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo + col0;
+          const bool col_ok = col0 < p.N;
+          if (col_ok) {
             const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              const float4 ba = __ldg(b4 + j / 4), bb = __ldg(b4 + j / 4 + 1);
-              float v[8] = {__uint_as_float(r[j + 0]) + ba.x, __uint_as_float(r[j + 1]) + ba.y,
-                            __uint_as_float(r[j + 2]) + ba.z, __uint_as_float(r[j + 3]) + ba.w,
-                            __uint_as_float(r[j + 4]) + bb.x, __uint_as_float(r[j + 5]) + bb.y,
-                            __uint_as_float(r[j + 6]) + bb.z, __uint_as_float(r[j + 7]) + bb.w};
+            for (int j4 = 0; j4 < 4; ++j4) {
+              const float4 bb = __ldg(b4 + j4);
+              float4 v = make_float4(__uint_as_float(r[4 * j4 + 0]) + bb.x, __uint_as_float(r[4 * j4 + 1]) + bb.y,
+                                     __uint_as_float(r[4 * j4 + 2]) + bb.z, __uint_as_float(r[4 * j4 + 3]) + bb.w);
               if constexpr (EPI == kBiasGelu) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = gelu_erf(v[k]);
+                v.x = gelu_erf(v.x);
+                v.y = gelu_erf(v.y);
+                v.z = gelu_erf(v.z);
+                v.w = gelu_erf(v.w);
               }
-              if (row_zero) {
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = 0.f;
-              }
-              uint4 o;
-              o.x = pack_half2(v[0], v[1]);
-              o.y = pack_half2(v[2], v[3]);
-              o.z = pack_half2(v[4], v[5]);
-              o.w = pack_half2(v[6], v[7]);
-              *reinterpret_cast<uint4*>(dst + j) = o;
+              my_row[j4 ^ ((lane >> 1) & 3)] = v;
             }
           }
+          __syncwarp();
+          if (col_ok) {
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+              const int rr = it * 8 + sub_row;
+              const int grow = m0 + quad * 32 + rr;
+              float4 v = reinterpret_cast<const float4*>(stage + rr * kStageCols)[sub_c4 ^ ((rr >> 1) & 3)];
+              if (grow < p.M) {
+                const int gcol = col0 + sub_c4 * 4;
+                bool zero = false;
+                if (p.row_len != nullptr) zero = (grow % p.seq_len) >= p.row_len[grow / p.seq_len];
+                if constexpr (EPI == kBiasResid) {
+                  // plain load: resid may alias sum_out
+                  const float4 rs = *reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(grow) * p.ld_resid + gcol);
+                  float4 sv = make_float4(rs.x + v.x, rs.y + v.y, rs.z + v.z, rs.w + v.w);
+                  if (zero) sv = make_float4(0.f, 0.f, 0.f, 0.f);
+                  *reinterpret_cast<float4*>(p.sum_out + static_cast<int64_t>(grow) * p.ld_sum + gcol) = sv;
+                } else {
+                  if (zero) v = make_float4(0.f, 0.f, 0.f, 0.f);
+                  uint2 o;
+                  o.x = pack_half2(v.x, v.y);
+                  o.y = pack_half2(v.z, v.w);
+                  *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + static_cast<int64_t>(grow) * p.ldo + gcol) = o;
+                }
+              }
+            }
+          }
+          __syncwarp();
         }
+        (void)row_zero;
       } else {
         // s = resid + acc + bias, written to sum_out (fp32). For kBiasResidLn
         // s is also written back into TMEM for the two statistic passes.

@@ -92,21 +92,12 @@ __device__ __forceinline__ bool row_is_padding(const Args& a, int64_t row) {
 
 // NV = groups of 4 columns per lane; d <= NV * 128.
 template <int NV, typename TX, typename TY, typename TS, typename TH>
-__global__ void __launch_bounds__(256) ln_warp_rows(Args a) {
+__global__ void __launch_bounds__(256, 3) ln_warp_rows(Args a) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   const int d = static_cast<int>(a.d);
   const float inv_d = 1.f / static_cast<float>(d);
-
-  float g[NV][4], b[NV][4];
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int c = (i * 32 + lane) * 4;
-    const int n = max(0, min(4, d - c));
-    Vec4<float>::load(a.gamma + c, a.vec, n, g[i]);
-    Vec4<float>::load(a.beta + c, a.vec, n, b[i]);
-  }
 
   for (int64_t row = warp; row < a.rows; row += nwarps) {
     const TX* xr = static_cast<const TX*>(a.x) + row * a.ld_x;
@@ -149,10 +140,14 @@ __global__ void __launch_bounds__(256) ln_warp_rows(Args a) {
     for (int i = 0; i < NV; ++i) {
       const int c = (i * 32 + lane) * 4;
       const int n = max(0, min(4, d - c));
-      float o[4];
+      if (n <= 0) continue;
+      // gamma/beta are re-read per row (L1-resident) to keep registers low
+      float g[4], b[4], o[4];
+      Vec4<float>::load(a.gamma + c, a.vec, n, g);
+      Vec4<float>::load(a.beta + c, a.vec, n, b);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) o[k] = pad ? 0.f : (v[i][k] - mean) * rstd * g[i][k] + b[i][k];
-      if (n > 0) Vec4<TH>::store(hr + c, a.vec, n, o);
+      for (int k = 0; k < 4; ++k) o[k] = pad ? 0.f : (v[i][k] - mean) * rstd * g[k] + b[k];
+      Vec4<TH>::store(hr + c, a.vec, n, o);
     }
   }
 }
