@@ -139,3 +139,29 @@ def test_cuda_graph_replay_matches_eager(cuda_device):
     for o in outs:
         torch.testing.assert_close(o, eager, atol=0, rtol=0)
     torch.testing.assert_close(other, eager2, atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 4])
+def test_forward_from_host_matches_device_forward(cuda_device, chunks):
+    cfg = StackConfig(6, 128, 256, 4, 512, 2, False)
+    _, model = build(cfg)
+    x, mask = generate_random_case(cfg, 11)
+    with torch.inference_mode():
+        want = model(x.cuda(), mask.cuda()).cpu()
+        out = model.forward_from_host(x.pin_memory(), mask, chunks=chunks)
+        torch.cuda.synchronize()
+        again = model.forward_from_host(x.pin_memory(), mask, chunks=chunks)  # slot reuse across calls
+        torch.cuda.synchronize()
+    torch.testing.assert_close(out, want, atol=0, rtol=0)
+    torch.testing.assert_close(again, want, atol=0, rtol=0)
+
+
+def test_forward_from_host_padded(cuda_device):
+    cfg = StackConfig(5, 64, 128, 4, 128, 1, True)
+    params, model = build(cfg)
+    x, mask = generate_random_case(cfg, 12, padding_ratio=0.4)
+    with torch.inference_mode():
+        out = model.forward_from_host(x.pin_memory(), mask, chunks=2)
+        torch.cuda.synchronize()
+    r = compare_outputs(stack_forward(params, cfg, x, mask), out)
+    assert r.passed, r

@@ -73,7 +73,34 @@ struct Cfg {
   static constexpr int SMEM_BYTES = LN_OFFSET + 2 * 2 * kBM * 4 + 1024 /*align*/;
 };
 
-__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); }
+// Exact-form GELU, x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)), as the harness's
+// F.gelu(approximate="none") (src/torch_transformer_benchmark.py:141).
+// erf is evaluated with Abramowitz & Stegun, Handbook of Mathematical
+// Functions, formula 7.1.26: for z >= 0,
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^{-z^2},  t = 1/(1 + p z),
+// |error| <= 1.5e-7, extended to z < 0 by oddness. The reciprocal and the
+// exponential use the SFU (rcp.approx, ex2.approx); the result is stored as
+// fp16 (relative rounding 2^-11), far above the approximation error. The
+// GEMM tests compare it with torch's exact erf GELU.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float gelu_erf(float v) {
+  constexpr float kP = 0.3275911f;
+  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f, kA4 = -1.453152027f,
+                  kA5 = 1.061405429f;
+  const float z = fabsf(v) * 0.70710678118654752f;
+  const float t = rcp_approx(fmaf(kP, z, 1.f));
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, kA5, kA4), kA3), kA2), kA1);
+  const float e = ex2_approx(-z * z * 1.4426950408889634f);
+  const float erf_abs = fmaf(-poly, e, 1.f);
+  const float half_x = 0.5f * v;
+  // 0.5 v (1 + sign(v) erf(|v|/sqrt2))
+  return fmaf(half_x, copysignf(erf_abs, v), half_x);
+}
 
 // wait sites (error word "where" low byte)
 enum : unsigned { kSiteEmpty = 1, kSiteFull = 2, kSiteAccEmpty = 3, kSiteAccFull = 4, kSiteDrain = 5, kSiteLn = 6 };

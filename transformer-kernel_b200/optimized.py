@@ -228,7 +228,7 @@ class OptimizedTransformer(nn.Module):
             tk.check_device_errors(x.device)
         return out if out.dtype == x.dtype else out.to(x.dtype)
 
-    def _run(self, x: torch.Tensor, lengths: Optional[torch.Tensor]) -> torch.Tensor:
+    def _run(self, x: torch.Tensor, lengths: Optional[torch.Tensor], out: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, S, d = x.shape
         T = B * S
         dev = x.device
@@ -246,7 +246,10 @@ class OptimizedTransformer(nn.Module):
         qkv = torch.empty((T, 3 * d), dtype=torch.float16, device=dev)
         ctx = torch.empty((B, S, d), dtype=torch.float16, device=dev)
         u = torch.empty((T, ffn), dtype=torch.float16, device=dev)
-        out = torch.empty((T, d), dtype=torch.float32, device=dev)
+        if out is None:
+            out = torch.empty((T, d), dtype=torch.float32, device=dev)
+        else:
+            out = out.view(T, d)
         stream = tk.stream_handle(dev)
 
         def layer_norm(src, w, b, eps, dst, zero_padded):
@@ -306,3 +309,86 @@ class OptimizedTransformer(nn.Module):
                         row_len=lengths, seq_len=seq)
                     run("ln", layer_norm, res, nw, nb, neps, dst, lengths is not None)
         return out.view(B, S, d)
+
+    # -- host-streamed forward --------------------------------------------------
+    def forward_from_host(
+        self,
+        x_host: torch.Tensor,
+        valid_token_mask: Optional[torch.Tensor] = None,
+        out_host: Optional[torch.Tensor] = None,
+        chunks: int = 4,
+        device: Optional[torch.device] = None,
+    ) -> torch.Tensor:
+        """Forward over a batch that lives in (pinned) host memory.
+
+        The batch is cut into ``chunks`` slices of whole sequences (rows are
+        independent, so slicing is exact). Three streams overlap the H2D
+        copy of slice i+1, the forward of slice i and the D2H copy of slice
+        i-1 -- the copy engines and the SMs work at the same time, where the
+        reference's out-of-core runner copies and computes in turn
+        (``src/run_case14.py:286-298``). Returns ``out_host`` (fp32, pinned);
+        it is complete once the current CUDA stream reaches the point where
+        this call returned (synchronise before reading it on the host).
+        """
+        if x_host.is_cuda:
+            raise ValueError("forward_from_host takes a host tensor; use forward() for device tensors")
+        if x_host.dim() != 3 or x_host.shape[-1] != self.d_model:
+            raise ValueError(f"expected x of shape [B, S, {self.d_model}], got {tuple(x_host.shape)}")
+        dev = device or self.layers[0].attention.q_proj.weight.device
+        if dev.type != "cuda":
+            raise tk.TKError("forward_from_host", -1, "the model must live on a CUDA device")
+        B, S, d = x_host.shape
+        if x_host.dtype != torch.float32:
+            x_host = x_host.float()
+        if out_host is None:
+            out_host = torch.empty((B, S, d), dtype=torch.float32, pin_memory=True)
+        lengths = self._prefix_lengths(valid_token_mask)
+        if lengths is not None:
+            lengths = lengths.to(dev)
+        n = max(1, min(int(chunks), B))
+        bounds = [B * i // n for i in range(n + 1)]
+        cb = max(bounds[i + 1] - bounds[i] for i in range(n))
+        key = (dev, S, d, cb)
+        ctx = getattr(self, "_stream_ctx", None)
+        if ctx is None or ctx["key"] != key:
+            with torch.cuda.device(dev):
+                ctx = {
+                    "key": key,
+                    "h2d": torch.cuda.Stream(dev),
+                    "d2h": torch.cuda.Stream(dev),
+                    "x": [torch.empty((cb, S, d), dtype=torch.float32, device=dev) for _ in range(2)],
+                    "out": [torch.empty((cb, S, d), dtype=torch.float32, device=dev) for _ in range(2)],
+                    "in_ready": [torch.cuda.Event() for _ in range(2)],
+                    "computed": [torch.cuda.Event() for _ in range(2)],
+                    "out_free": [torch.cuda.Event() for _ in range(2)],
+                }
+            self._stream_ctx = ctx
+        compute = torch.cuda.current_stream(dev)
+        h2d, d2h = ctx["h2d"], ctx["d2h"]
+        # slots may still be in use by a previous call on the compute stream
+        h2d.wait_stream(compute)
+        d2h.wait_stream(compute)
+        with torch.cuda.device(dev):
+            for i in range(n):
+                s, b0, b1 = i % 2, bounds[i], bounds[i + 1]
+                nb = b1 - b0
+                xs, os_ = ctx["x"][s][:nb], ctx["out"][s][:nb]
+                with torch.cuda.stream(h2d):
+                    if i >= 2:
+                        h2d.wait_event(ctx["computed"][s])  # forward i-2 done reading the slot
+                    xs.copy_(x_host[b0:b1], non_blocking=True)
+                    ctx["in_ready"][s].record(h2d)
+                compute.wait_event(ctx["in_ready"][s])
+                if i >= 2:
+                    compute.wait_event(ctx["out_free"][s])  # D2H i-2 done reading the slot
+                self._run(xs, None if lengths is None else lengths[b0:b1], out=os_)
+                ctx["computed"][s].record(compute)
+                with torch.cuda.stream(d2h):
+                    d2h.wait_event(ctx["computed"][s])
+                    out_host[b0:b1].copy_(os_, non_blocking=True)
+                    ctx["out_free"][s].record(d2h)
+            compute.wait_stream(d2h)
+            compute.wait_stream(h2d)
+        if self.settings.check_device_errors:
+            tk.check_device_errors(dev)
+        return out_host
