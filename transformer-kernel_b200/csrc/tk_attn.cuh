@@ -246,7 +246,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t sv[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(t_lane + c * 32, sv[c]);
-      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);  // first waits, the rest only pin registers
       // Masking is only needed on the causal diagonal tile and the tile
       // holding the kv bound; `full` is warp-uniform elsewhere.
       const bool full = lim >= kBN;
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < HD; c += 16) {
           uint32_t o[16];
           tmem_ld16(t_lane + kColO + c, o);
-          tmem_ld_wait();
+          tmem_ld_wait(o);
 #pragma unroll
           for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
           tmem_st16(t_lane + kColO + c, o);
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint32_t o[16];
         if (n_kv > 0) {
           tmem_ld16(t_lane + kColO + c, o);
-          tmem_ld_wait();
+          tmem_ld_wait(o);
         } else {
 #pragma unroll
           for (int t = 0; t < 16; ++t) o[t] = 0u;

@@ -273,47 +273,65 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* stage = reinterpret_cast<float*>(smem + C::EPI_OFFSET) + (warp - 2) * (32 * kStageCols);
         float4* my_row = reinterpret_cast<float4*>(stage + lane * kStageCols);
         const int sub_row = static_cast<int>(lane >> 2), sub_c4 = static_cast<int>(lane & 3);
-#pragma unroll 1
-        for (int c = 0; c < HALF_N; c += kStageCols) {
-          uint32_t r[16];
-          tmem_ld16(t_row + c, r);
-          tmem_ld_wait();
-          const int col0 = n0 + half * HALF_N + c;
-          const bool col_ok = col0 < p.N;
-          if (col_ok) {
-            const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+        constexpr int kChunks = HALF_N / kStageCols;
+        const int col_base = n0 + half * HALF_N;
+        // Residual rows of chunk c in the transposed layout, fetched one
+        // chunk ahead so the loads overlap the previous chunk's work.
+        auto load_resid = [&](int c, float4 (&dst)[4]) {
+          const int gcol = col_base + c * kStageCols + sub_c4 * 4;
 #pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4) {
-              const float4 bb = __ldg(b4 + j4);
-              float4 v = make_float4(__uint_as_float(r[4 * j4 + 0]) + bb.x, __uint_as_float(r[4 * j4 + 1]) + bb.y,
-                                     __uint_as_float(r[4 * j4 + 2]) + bb.z, __uint_as_float(r[4 * j4 + 3]) + bb.w);
-              if constexpr (EPI == kBiasGelu) {
-                v.x = gelu_erf(v.x);
-                v.y = gelu_erf(v.y);
-                v.z = gelu_erf(v.z);
-                v.w = gelu_erf(v.w);
-              }
-              my_row[j4 ^ ((lane >> 1) & 3)] = v;
-            }
+          for (int it = 0; it < 4; ++it) {
+            const int grow = m0 + quad * 32 + it * 8 + sub_row;
+            // plain load: resid may alias sum_out
+            dst[it] = (grow < p.M && gcol < p.N)
+                          ? *reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(grow) * p.ld_resid + gcol)
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
           }
+        };
+        float4 res_cur[4], res_nxt[4];
+        if constexpr (EPI == kBiasResid) load_resid(0, res_cur);
+        uint32_t r[16];
+        tmem_ld16(t_row, r);
+        tmem_ld_wait(r);
+#pragma unroll 1
+        for (int c = 0; c < kChunks; ++c) {
+          const int col0 = col_base + c * kStageCols;
+          const bool col_ok = col0 < p.N;
+          // raw accumulators, thread = row, into the swizzled staging tile
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4)
+            my_row[j4 ^ ((lane >> 1) & 3)] =
+                make_float4(__uint_as_float(r[4 * j4 + 0]), __uint_as_float(r[4 * j4 + 1]),
+                            __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
           __syncwarp();
+          if (c + 1 < kChunks) {
+            tmem_ld16(t_row + (c + 1) * kStageCols, r);  // in flight during this chunk
+            if constexpr (EPI == kBiasResid) load_resid(c + 1, res_nxt);
+          }
           if (col_ok) {
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + sub_c4);
 #pragma unroll
             for (int it = 0; it < 4; ++it) {
               const int rr = it * 8 + sub_row;
               const int grow = m0 + quad * 32 + rr;
-              float4 v = reinterpret_cast<const float4*>(stage + rr * kStageCols)[sub_c4 ^ ((rr >> 1) & 3)];
+              const float4 a = reinterpret_cast<const float4*>(stage + rr * kStageCols)[sub_c4 ^ ((rr >> 1) & 3)];
+              float4 v = make_float4(a.x + bb.x, a.y + bb.y, a.z + bb.z, a.w + bb.w);
               if (grow < p.M) {
                 const int gcol = col0 + sub_c4 * 4;
                 bool zero = false;
                 if (p.row_len != nullptr) zero = (grow % p.seq_len) >= p.row_len[grow / p.seq_len];
                 if constexpr (EPI == kBiasResid) {
-                  // plain load: resid may alias sum_out
-                  const float4 rs = *reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(grow) * p.ld_resid + gcol);
+                  const float4 rs = res_cur[it];
                   float4 sv = make_float4(rs.x + v.x, rs.y + v.y, rs.z + v.z, rs.w + v.w);
                   if (zero) sv = make_float4(0.f, 0.f, 0.f, 0.f);
                   *reinterpret_cast<float4*>(p.sum_out + static_cast<int64_t>(grow) * p.ld_sum + gcol) = sv;
                 } else {
+                  if constexpr (EPI == kBiasGelu) {
+                    v.x = gelu_erf(v.x);
+                    v.y = gelu_erf(v.y);
+                    v.z = gelu_erf(v.z);
+                    v.w = gelu_erf(v.w);
+                  }
                   if (zero) v = make_float4(0.f, 0.f, 0.f, 0.f);
                   uint2 o;
                   o.x = pack_half2(v.x, v.y);
@@ -324,6 +342,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           __syncwarp();
+          if (c + 1 < kChunks) {
+            tmem_ld_wait(r);
+            if constexpr (EPI == kBiasResid) {
+#pragma unroll
+              for (int it = 0; it < 4; ++it) res_cur[it] = res_nxt[it];
+            }
+          }
         }
         (void)row_zero;
       } else {
@@ -334,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < HALF_N; c += 32) {
           uint32_t r[32];
           tmem_ld32(t_row + c, r);
-          tmem_ld_wait();
+          tmem_ld_wait(r);
           const int col0 = n0 + half * HALF_N + c;
           if (row_ok && col0 < p.N) {
             const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
@@ -387,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < HALF_N; c += 32) {
             uint32_t r[32];
             tmem_ld32(t_row + c, r);
-            tmem_ld_wait();
+            tmem_ld_wait(r);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float t = __uint_as_float(r[j]) - mean;
@@ -408,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < HALF_N; c += 32) {
             uint32_t r[32];
             tmem_ld32(t_row + c, r);
-            tmem_ld_wait();
+            tmem_ld_wait(r);
             const int col0 = n0 + half * HALF_N + c;
             if (row_ok) {
               const float4* g4 = reinterpret_cast<const float4*>(p.gamma + col0);
