@@ -124,3 +124,33 @@ def test_gemm_output_guard_bands(cuda_device):
     torch.cuda.synchronize()
     assert torch.all(buf[:pad] == 123.0) and torch.all(buf[-pad:] == 123.0)
     torch.testing.assert_close(out.float().cpu(), ref_linear(a, w, b), atol=2e-3, rtol=2e-2)
+
+
+# Shapes with N % 256 == 0 and >= 148 tiles of 256 x 256 take the CTA-pair
+# (tcgen05 cta_group::2) kernel; the M tails leave the odd CTA of the last
+# pair partly (9000) or entirely (8320) out of range.
+PAIR_SHAPES = [(8192, 3072, 1024), (9000, 2048, 512), (8320, 4096, 256)]
+
+
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES)
+def test_gemm_pair_bias(cuda_device, M, N, K):
+    a, w, b = operands(M, N, K, seed=31)
+    out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "bias")
+    torch.testing.assert_close(out.float().cpu(), ref_linear(a, w, b), atol=2e-3, rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K", PAIR_SHAPES[1:])
+def test_gemm_pair_gelu(cuda_device, M, N, K):
+    a, w, b = operands(M, N, K, seed=37)
+    out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "gelu")
+    want = F.gelu(ref_linear(a, w, b), approximate="none")
+    torch.testing.assert_close(out.float().cpu(), want, atol=2e-4, rtol=1e-3)
+
+
+@pytest.mark.parametrize("M,N,K", [(16384, 1024, 1024), (9000, 2048, 512)])
+def test_gemm_pair_resid_in_place(cuda_device, M, N, K):
+    a, w, b = operands(M, N, K, seed=41)
+    r = seeded(M, N, seed=42)
+    buf = r.cuda()
+    tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid", resid=buf, sum_out=buf)
+    torch.testing.assert_close(buf.cpu(), r + ref_linear(a, w, b), atol=1e-4, rtol=1e-4)

@@ -135,6 +135,35 @@ int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mw, const
   return fail(TK_ERR_INVALID, "unknown epilogue %d", epi);
 }
 
+template <int EPI>
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mw, const tk::gemm::Params& p, DeviceInfo* info,
+                     cudaStream_t stream) {
+  using C = tk::gemm::PairCfg;
+  auto kern = tk::gemm::gemm_pair_kernel<EPI>;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!info->gemm_attr_set[3][EPI]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm pair smem)");
+      info->gemm_attr_set[3][EPI] = true;
+    }
+  }
+  const int tiles = ((p.M + 255) / 256) * (p.N / 256);
+  const int pairs = tiles < info->sms / 2 ? tiles : info->sms / 2;
+  kern<<<2 * pairs, tk::gemm::kThreads, C::SMEM_BYTES, stream>>>(ma, mw, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
+  return TK_OK;
+}
+
+// The CTA-pair kernel (256 x 256 tiles over two SMs) for non-LN epilogues
+// with N % 256 == 0 and at least two waves of pair tiles.
+bool use_pair(int epi, int64_t M, int64_t N, int sms) {
+  if (epi == TK_EPI_BIAS_RESID_LN || N % 256 != 0) return false;
+  const int64_t tiles = ((M + 255) / 256) * (N / 256);
+  return tiles >= sms;
+}
+
 // Tile width: the fused-LN epilogue needs the whole row in one tile; else the
 // widest tile that still gives every SM at least one tile.
 int pick_bn(int epi, int64_t M, int64_t N, int sms) {
@@ -268,7 +297,8 @@ int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
   int dev;
   DeviceInfo* info;
   if (int st = current_device(&dev, &info)) return st;
-  const int bn = pick_bn(epilogue, M, N, info->sms);
+  const bool pair = use_pair(epilogue, M, N, info->sms);
+  const int bn = pair ? 128 : pick_bn(epilogue, M, N, info->sms);  // pair: each CTA stages 128 rows of W
   if (bn == 0) return fail(TK_ERR_UNSUPPORTED, "tk_gemm: N=%lld has no tile width", (long long)N);
 
   CUtensorMap ma, mw;
@@ -292,6 +322,13 @@ int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
   p.row_len = row_len; p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : 1);
   p.wait_limit_ns = g_wait_limit_ns.load();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pair) {
+    switch (epilogue) {
+      case TK_EPI_BIAS: return launch_gemm_pair<tk::gemm::kBias>(ma, mw, p, info, s);
+      case TK_EPI_BIAS_GELU: return launch_gemm_pair<tk::gemm::kBiasGelu>(ma, mw, p, info, s);
+      case TK_EPI_BIAS_RESID: return launch_gemm_pair<tk::gemm::kBiasResid>(ma, mw, p, info, s);
+    }
+  }
   switch (bn) {
     case 64: return launch_gemm_epi<64>(epilogue, ma, mw, p, info, s);
     case 128: return launch_gemm_epi<128>(epilogue, ma, mw, p, info, s);

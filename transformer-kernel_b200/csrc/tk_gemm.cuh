@@ -102,6 +102,97 @@ __device__ __forceinline__ float gelu_erf(float v) {
   return fmaf(half_x, copysignf(erf_abs, v), half_x);
 }
 
+// Non-LayerNorm epilogue of one 32-row x HALF_N-column slice of an
+// accumulator tile, run by one epilogue warp. Thread-per-row TMEM chunks go
+// through a swizzled 2 KB staging tile so that bias / residual / output
+// global traffic runs along rows (lane -> row it*8 + lane/4, float4 column
+// lane%4). `row_base` is the first global row of the warp's 32 TMEM lanes,
+// `col_base` the first global column of the slice.
+template <int HALF_N, int EPI>
+__device__ __forceinline__ void staged_epilogue(const Params& p, float* stage, uint32_t t_row, int row_base,
+                                                int col_base, uint32_t lane) {
+    // Thread-per-row TMEM chunk -> swizzled staging -> row-contiguous
+    // global traffic (lane -> row it*8 + lane/4, float4 column lane%4).
+    float4* my_row = reinterpret_cast<float4*>(stage + lane * kStageCols);
+    const int sub_row = static_cast<int>(lane >> 2), sub_c4 = static_cast<int>(lane & 3);
+    constexpr int kChunks = HALF_N / kStageCols;
+    // Residual rows of chunk c in the transposed layout, fetched one
+    // chunk ahead so the loads overlap the previous chunk's work.
+    auto load_resid = [&](int c, float4 (&dst)[4]) {
+      const int gcol = col_base + c * kStageCols + sub_c4 * 4;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int grow = row_base + it * 8 + sub_row;
+        // plain load: resid may alias sum_out
+        dst[it] = (grow < p.M && gcol < p.N)
+                      ? *reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(grow) * p.ld_resid + gcol)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    float4 res_cur[4], res_nxt[4];
+    if constexpr (EPI == kBiasResid) load_resid(0, res_cur);
+    uint32_t r[16];
+    tmem_ld16(t_row, r);
+    tmem_ld_wait(r);
+#pragma unroll 1
+    for (int c = 0; c < kChunks; ++c) {
+      const int col0 = col_base + c * kStageCols;
+      const bool col_ok = col0 < p.N;
+      // raw accumulators, thread = row, into the swizzled staging tile
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4)
+        my_row[j4 ^ ((lane >> 1) & 3)] =
+            make_float4(__uint_as_float(r[4 * j4 + 0]), __uint_as_float(r[4 * j4 + 1]),
+                        __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
+      __syncwarp();
+      if (c + 1 < kChunks) {
+        tmem_ld16(t_row + (c + 1) * kStageCols, r);  // in flight during this chunk
+        if constexpr (EPI == kBiasResid) load_resid(c + 1, res_nxt);
+      }
+      if (col_ok) {
+        const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + sub_c4);
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int rr = it * 8 + sub_row;
+          const int grow = row_base + rr;
+          const float4 a = reinterpret_cast<const float4*>(stage + rr * kStageCols)[sub_c4 ^ ((rr >> 1) & 3)];
+          float4 v = make_float4(a.x + bb.x, a.y + bb.y, a.z + bb.z, a.w + bb.w);
+          if (grow < p.M) {
+            const int gcol = col0 + sub_c4 * 4;
+            bool zero = false;
+            if (p.row_len != nullptr) zero = (grow % p.seq_len) >= p.row_len[grow / p.seq_len];
+            if constexpr (EPI == kBiasResid) {
+              const float4 rs = res_cur[it];
+              float4 sv = make_float4(rs.x + v.x, rs.y + v.y, rs.z + v.z, rs.w + v.w);
+              if (zero) sv = make_float4(0.f, 0.f, 0.f, 0.f);
+              *reinterpret_cast<float4*>(p.sum_out + static_cast<int64_t>(grow) * p.ld_sum + gcol) = sv;
+            } else {
+              if constexpr (EPI == kBiasGelu) {
+                v.x = gelu_erf(v.x);
+                v.y = gelu_erf(v.y);
+                v.z = gelu_erf(v.z);
+                v.w = gelu_erf(v.w);
+              }
+              if (zero) v = make_float4(0.f, 0.f, 0.f, 0.f);
+              uint2 o;
+              o.x = pack_half2(v.x, v.y);
+              o.y = pack_half2(v.z, v.w);
+              *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + static_cast<int64_t>(grow) * p.ldo + gcol) = o;
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (c + 1 < kChunks) {
+        tmem_ld_wait(r);
+        if constexpr (EPI == kBiasResid) {
+#pragma unroll
+          for (int it = 0; it < 4; ++it) res_cur[it] = res_nxt[it];
+        }
+      }
+    }
+}
+
 // wait sites (error word "where" low byte)
 enum : unsigned { kSiteEmpty = 1, kSiteFull = 2, kSiteAccEmpty = 3, kSiteAccFull = 4, kSiteDrain = 5, kSiteLn = 6 };
 
@@ -268,88 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * BN + half * HALF_N;
 
       if constexpr (EPI != kBiasResidLn) {
-        // Thread-per-row TMEM chunk -> swizzled staging -> row-contiguous
-        // global traffic (lane -> row it*8 + lane/4, float4 column lane%4).
         float* stage = reinterpret_cast<float*>(smem + C::EPI_OFFSET) + (warp - 2) * (32 * kStageCols);
-        float4* my_row = reinterpret_cast<float4*>(stage + lane * kStageCols);
-        const int sub_row = static_cast<int>(lane >> 2), sub_c4 = static_cast<int>(lane & 3);
-        constexpr int kChunks = HALF_N / kStageCols;
-        const int col_base = n0 + half * HALF_N;
-        // Residual rows of chunk c in the transposed layout, fetched one
-        // chunk ahead so the loads overlap the previous chunk's work.
-        auto load_resid = [&](int c, float4 (&dst)[4]) {
-          const int gcol = col_base + c * kStageCols + sub_c4 * 4;
-#pragma unroll
-          for (int it = 0; it < 4; ++it) {
-            const int grow = m0 + quad * 32 + it * 8 + sub_row;
-            // plain load: resid may alias sum_out
-            dst[it] = (grow < p.M && gcol < p.N)
-                          ? *reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(grow) * p.ld_resid + gcol)
-                          : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-        };
-        float4 res_cur[4], res_nxt[4];
-        if constexpr (EPI == kBiasResid) load_resid(0, res_cur);
-        uint32_t r[16];
-        tmem_ld16(t_row, r);
-        tmem_ld_wait(r);
-#pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
-          const int col0 = col_base + c * kStageCols;
-          const bool col_ok = col0 < p.N;
-          // raw accumulators, thread = row, into the swizzled staging tile
-#pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4)
-            my_row[j4 ^ ((lane >> 1) & 3)] =
-                make_float4(__uint_as_float(r[4 * j4 + 0]), __uint_as_float(r[4 * j4 + 1]),
-                            __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
-          __syncwarp();
-          if (c + 1 < kChunks) {
-            tmem_ld16(t_row + (c + 1) * kStageCols, r);  // in flight during this chunk
-            if constexpr (EPI == kBiasResid) load_resid(c + 1, res_nxt);
-          }
-          if (col_ok) {
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + sub_c4);
-#pragma unroll
-            for (int it = 0; it < 4; ++it) {
-              const int rr = it * 8 + sub_row;
-              const int grow = m0 + quad * 32 + rr;
-              const float4 a = reinterpret_cast<const float4*>(stage + rr * kStageCols)[sub_c4 ^ ((rr >> 1) & 3)];
-              float4 v = make_float4(a.x + bb.x, a.y + bb.y, a.z + bb.z, a.w + bb.w);
-              if (grow < p.M) {
-                const int gcol = col0 + sub_c4 * 4;
-                bool zero = false;
-                if (p.row_len != nullptr) zero = (grow % p.seq_len) >= p.row_len[grow / p.seq_len];
-                if constexpr (EPI == kBiasResid) {
-                  const float4 rs = res_cur[it];
-                  float4 sv = make_float4(rs.x + v.x, rs.y + v.y, rs.z + v.z, rs.w + v.w);
-                  if (zero) sv = make_float4(0.f, 0.f, 0.f, 0.f);
-                  *reinterpret_cast<float4*>(p.sum_out + static_cast<int64_t>(grow) * p.ld_sum + gcol) = sv;
-                } else {
-                  if constexpr (EPI == kBiasGelu) {
-                    v.x = gelu_erf(v.x);
-                    v.y = gelu_erf(v.y);
-                    v.z = gelu_erf(v.z);
-                    v.w = gelu_erf(v.w);
-                  }
-                  if (zero) v = make_float4(0.f, 0.f, 0.f, 0.f);
-                  uint2 o;
-                  o.x = pack_half2(v.x, v.y);
-                  o.y = pack_half2(v.z, v.w);
-                  *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + static_cast<int64_t>(grow) * p.ldo + gcol) = o;
-                }
-              }
-            }
-          }
-          __syncwarp();
-          if (c + 1 < kChunks) {
-            tmem_ld_wait(r);
-            if constexpr (EPI == kBiasResid) {
-#pragma unroll
-              for (int it = 0; it < 4; ++it) res_cur[it] = res_nxt[it];
-            }
-          }
-        }
+        staged_epilogue<HALF_N, EPI>(p, stage, t_row, m0 + quad * 32, n0 + half * HALF_N, lane);
         (void)row_zero;
       } else {
         // s = resid + acc + bias, written to sum_out (fp32). For kBiasResidLn
@@ -481,6 +492,192 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ----------------------------------------------------------------------------
+// CTA-pair variant: a 2-CTA cluster computes 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2 (M = 256 across the pair's TMEM, N = 256). Each
+// CTA stages its own 128 rows of A and its own half (128 rows) of W, so a
+// k-block costs each SM 32 KB of shared memory instead of 48 KB for the same
+// MMA work, and the stage ring is 6 deep. The even CTA issues every MMA;
+// both CTAs' TMA loads complete on the even CTA's stage barrier, and each
+// MMA commit is delivered to both CTAs. Epilogues are per CTA (its 128 rows),
+// identical to the single-CTA kernel. Non-LayerNorm epilogues, N % 256 == 0.
+// ----------------------------------------------------------------------------
+struct PairCfg {
+  static constexpr int A_BYTES = 128 * kBK * 2;
+  static constexpr int B_BYTES = 128 * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = EPI_OFFSET + kEpiWarps * kStageBytesPerWarp + 1024;
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, Params p) {
+  static_assert(EPI != kBiasResidLn, "pair kernel has no LayerNorm epilogue");
+  using C = PairCfg;
+  constexpr int TN = 256;  // pair tile: 256 rows x 256 columns
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];   // used in the even CTA
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];          // used in the even CTA
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = warp_id_uniform();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+  const int m_tiles = (p.M + 2 * kBM - 1) / (2 * kBM);
+  const int n_tiles = p.N / TN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+  const unsigned kid = 0x40u + EPI;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barrier inits and TMEM allocation visible to the peer
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&map_a);
+      prefetch_tensormap(&map_w);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int m0 = (tile / n_tiles) * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = (tile % n_tiles) * TN + static_cast<int>(rank) * (TN / 2);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteEmpty);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
+          const uint32_t full_even = mapa_shared(&full_bar[stage], 0);
+          tma_load_2d_pair(sa, &map_a, full_even, kb * kBK, m0);
+          tma_load_2d_pair(sb, &map_w, full_even, kb * kBK, n0);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      (void)ok;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (even CTA) ----------------
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(2 * kBM, TN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
+          report_error(kDevWaitTimeout, kid * 256 + kSiteAccEmpty);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * TN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait_cluster(&full_bar[stage], phase, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteFull);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
+            const uint64_t db = smem_desc(b_addr + kk * 32, 16, 1024, kLayoutSW128);
+            mma_f16_ss_pair(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(mapa_shared(&empty_bar[stage], 0));
+          mma_commit_pair(mapa_shared(&empty_bar[stage], 1));
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) {
+          mma_commit_pair(mapa_shared(&acc_full[acc], 0));
+          mma_commit_pair(mapa_shared(&acc_full[acc], 1));
+        }
+      }
+      mma_commit_pair(mapa_shared(&drain_bar, 0));
+      if (!mbar_wait_cluster(&drain_bar, 0, nullptr, p.wait_limit_ns) && ok)
+        report_error(kDevWaitTimeout, kid * 256 + kSiteDrain);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (both CTAs, own 128 rows) ----------------
+    const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int HALF_N = TN / 2;
+    float* stage = reinterpret_cast<float*>(smem + C::EPI_OFFSET) + (warp - 2) * (32 * kStageCols);
+    int it = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, &abort_flag, p.wait_limit_ns)) {
+        report_error(kDevWaitTimeout, kid * 256 + kSiteAccFull);
+        abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (tile / n_tiles) * 2 * kBM + static_cast<int>(rank) * kBM;
+      const int n0 = (tile % n_tiles) * TN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * TN + half * HALF_N;
+      staged_epilogue<HALF_N, EPI>(p, stage, t_row, m0 + quad * 32, n0 + half * HALF_N, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's TMEM is written by the even CTA's MMAs
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
 }
 
 }  // namespace gemm
