@@ -74,7 +74,7 @@ def attn_flops(B, S, H, hd, causal):
 class Clocks:
     """Samples SM clocks and throttle reasons with nvidia-smi while timing."""
 
-    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+    FIELDS = "timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
@@ -90,7 +90,7 @@ class Clocks:
             # -f writes each sample straight to the file (a pipe would be
             # block-buffered and lost when the sampler is stopped).
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.index), "-f", self.path],
                 stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
             time.sleep(0.5)  # first sample lands before the timed region
@@ -114,25 +114,40 @@ class Clocks:
             except OSError:
                 self.lines = []
 
+    def mark(self, which: str) -> None:
+        """Record the host time at the start / end of the timed region."""
+        setattr(self, which, time.time())
+
     def summary(self):
-        sms, maxes, reasons = [], [], set()
+        """Median SM clock and throttle reasons over the samples taken inside
+        the timed region (marked with mark('t_start') / mark('t_end'))."""
+        import datetime
+
+        lo = getattr(self, "t_start", 0.0) - 0.05
+        hi = getattr(self, "t_end", float("inf")) + 0.05
+        sms, maxes, reasons, outside = [], [], set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sms.append(float(f[1]))
-                maxes.append(float(f[2]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                sm, smax = float(f[2]), float(f[3])
             except ValueError:
                 continue
-            for name, flag in zip(names, f[5:9]):
+            if not (lo <= ts <= hi):
+                outside += 1
+                continue
+            sms.append(sm)
+            maxes.append(smax)
+            for name, flag in zip(names, f[6:10]):
                 if flag.lower() == "active":
                     reasons.add(name)
         if not sms:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
-                "samples": len(sms)}
+                "samples": len(sms), "period_ms": 50}
 
 
 def cpu_forward_rate(cfg_tuple, seconds, sample_batch, steps=None):
@@ -189,7 +204,7 @@ def run_reference(args, cfg_tuple, rank):
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="C3", choices=sorted(CONFIGS))
     ap.add_argument("--batch", type=int, default=0, help="override the config's batch (small profiling cases)")
@@ -261,11 +276,13 @@ def main() -> int:
         torch.cuda.synchronize(dev)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with Clocks(local) as clk:
+            clk.mark("t_start")
             t0.record(stream)
             for _ in range(args.steps):
                 model(x, mask)
             t1.record(stream)
             torch.cuda.synchronize(dev)
+            clk.mark("t_end")
         barrier()
         ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
         clocks = clk.summary()
