@@ -1,4 +1,4 @@
-// Blackwell flash-attention forward over the fused QKV buffer.
+// Blackwell flash-attention forward.
 //
 // Replaces the reference's attention (F.scaled_dot_product_attention,
 // src/optimized.py:615-624, and the Triton FA2 kernel src/kernels.py:136-247)
@@ -17,16 +17,20 @@
 // projection (head stride hd < row stride 3d), {hd, S, H, B} for [B,H,S,hd]
 // contiguous tensors.
 //
-// Per CTA: one (b, h, 128-query tile). Warp 0 issues TMA, warp 1 owns TMEM
-// and issues tcgen05.mma, warps 2..5 (one TMEM lane quadrant each, one query
-// row per thread) run the softmax. TMEM (256 columns): S = Q K^T in columns
-// [0,128) fp32; P = softmax numerators as packed fp16 pairs written back over
-// S columns [0,64); O in columns [128, 128+HD) fp32.
-//   S_j   : tcgen05.mma SS, M=128 N=128 K=16 x (HD/16)         (A=Q, B=K, both K-major)
-//   O    += P_j V_j : tcgen05.mma TS, M=128 N=HD K=16 x 8      (A=P from TMEM, B=V MN-major)
-// tcgen05.mma issued by one thread execute in order, so S_{j+1} (which
-// overwrites P_j) is issued only after PV_j, and the completion of S_{j+1}
-// also tells the softmax warps that PV_j has finished with O.
+// One CTA per (b, h, pair of 128-query tiles), one CTA per SM. Warp roles:
+// warp 0 TMA, warp 1 TMEM owner + MMA issuer, warps 2..5 softmax group 0
+// (query tile 2p), warps 6..9 softmax group 1 (tile 2p+1); each softmax
+// thread owns one query row (its warp's TMEM lane quadrant). Both groups
+// share every K/V tile. TMEM (512 columns): S_g = Q_g K^T in columns
+// [128g, 128g+128) fp32, P_g = softmax numerators as packed fp16 pairs over
+// S_g columns [128g, 128g+64), O_g in columns [256+128g, 256+128g+HD).
+//   S_g(j) : tcgen05.mma SS, M=128 N=128 K=16 x (HD/16)     (A=Q_g, B=K_j, both K-major)
+//   O_g   += P_g(j) V_j : tcgen05.mma TS, M=128 N=HD K=16 x 8 (A=P_g in TMEM, B=V_j MN-major)
+// The MMA warp issues S0(0) S1(0) | PV0(0) S0(1) | PV1(0) S1(1) | PV0(1) ...
+// so one group's softmax runs while the tensor core works for the other.
+// tcgen05.mma from one thread execute in order: S_g(j+1) (which overwrites
+// P_g(j)) follows PV_g(j), and the completion of S_g(j+1) tells group g that
+// PV_g(j) has finished with O_g.
 //
 // Online softmax keeps the running max m in raw-score units and rescales
 // O and l only when the max grows by more than 2^8 in the exponent (lazy
@@ -42,12 +46,12 @@
 namespace tk {
 namespace attn {
 
-constexpr int kBM = 128;  // queries per CTA
+constexpr int kBM = 128;  // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;  // keys per KV tile
-constexpr int kThreads = 192;
-constexpr int kStages = 2;
-constexpr int kTmemCols = 256;
-constexpr int kColO = 128;
+constexpr int kThreads = 320;
+constexpr int kStages = 4;
+constexpr int kTmemCols = 512;
+constexpr int kColO = 256;
 constexpr float kLazyRescaleLog2 = 8.f;
 
 struct Params {
@@ -77,13 +81,39 @@ struct Cfg {
   static constexpr SmemLayout LAYOUT = HD == 64 ? kLayoutSW128 : kLayoutSW64;
   static constexpr int TILE_BYTES = kBM * ROW_BYTES;           // Q, K or V tile
   static constexpr int SBO = 8 * ROW_BYTES;                    // 8-row core-matrix group
-  static constexpr int SMEM_BYTES = TILE_BYTES * (1 + 2 * kStages) + 1024;
+  static constexpr int SMEM_BYTES = TILE_BYTES * (2 + 2 * kStages) + 1024;
 };
+
+// ---- packed fp32 helpers (sm_100 f32x2 FMA/ADD, 3-input max) ----
+__device__ __forceinline__ void fma2(float& r0, float& r1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 ra, rs;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rs, {%0, %1};\n\t"
+      "add.rn.f32x2 rs, rs, ra;\n\t"
+      "mov.b64 {%0, %1}, rs;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 
 enum : unsigned { kSiteQ = 1, kSiteKV = 2, kSiteS = 3, kSiteP = 4, kSiteO = 5, kSiteEmpty = 6, kSiteDrain = 7 };
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, Params p) {
   using C = Cfg<HD>;
@@ -91,29 +121,36 @@ __global__ void __launch_bounds__(kThreads, 2)
   __shared__ __align__(8) uint64_t q_full;
   __shared__ __align__(8) uint64_t kv_full[kStages];
   __shared__ __align__(8) uint64_t kv_empty[kStages];
-  __shared__ __align__(8) uint64_t s_full;
-  __shared__ __align__(8) uint64_t p_full;
+  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t p_full[2];
   __shared__ __align__(8) uint64_t o_full;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + C::TILE_BYTES;                           // kStages tiles
-  uint8_t* sV = smem + C::TILE_BYTES * (1 + kStages);           // kStages tiles
+  uint8_t* sQ = smem;                                   // 2 tiles
+  uint8_t* sK = smem + 2 * C::TILE_BYTES;               // kStages tiles
+  uint8_t* sV = smem + C::TILE_BYTES * (2 + kStages);   // kStages tiles
 
   const int warp = warp_id_uniform();
   const uint32_t lane = lane_id();
   const int q_tiles = (p.S + kBM - 1) / kBM;
+  const int q_pairs = (q_tiles + 1) / 2;
   const int bh_count = p.B * p.H;
-  // Heaviest (last, for causal) query tiles are launched first.
-  const int qt = q_tiles - 1 - static_cast<int>(blockIdx.x / bh_count);
+  // Heaviest (last, for causal) tile pairs are launched first.
+  const int qp = q_pairs - 1 - static_cast<int>(blockIdx.x / bh_count);
   const int bh = static_cast<int>(blockIdx.x % bh_count);
   const int b = bh / p.H, h = bh % p.H;
+  const int tq[2] = {2 * qp, 2 * qp + 1};
+  const bool has1 = tq[1] < q_tiles;
   int kv_bound = p.S;
   if (p.kv_len != nullptr) kv_bound = max(0, min(p.S, p.kv_len[b]));
-  int n_kv = (kv_bound + kBN - 1) / kBN;
-  if (p.causal) n_kv = min(n_kv, qt + 1);
+  const int n_all = (kv_bound + kBN - 1) / kBN;
+  // number of KV tiles each group attends to
+  int last[2];
+  last[0] = p.causal ? min(n_all, tq[0] + 1) : n_all;
+  last[1] = has1 ? (p.causal ? min(n_all, tq[1] + 1) : n_all) : 0;
+  const int n_kv = max(last[0], last[1]);
   const unsigned kid = 0x80u + HD;
 
   if (threadIdx.x == 0) {
@@ -122,8 +159,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(&s_full, 1);
-    mbar_init(&p_full, 4);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&p_full[g], 4);
+    }
     mbar_init(&o_full, 1);
     abort_flag = 0;
     fence_barrier_init();
@@ -143,8 +182,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      mbar_arrive_expect_tx(&q_full, C::TILE_BYTES);
-      load_tile(sQ, &map_q, &q_full, p, qt * kBM, h, b);
+      mbar_arrive_expect_tx(&q_full, C::TILE_BYTES * (has1 ? 2 : 1));
+      load_tile(sQ, &map_q, &q_full, p, tq[0] * kBM, h, b);
+      if (has1) load_tile(sQ + C::TILE_BYTES, &map_q, &q_full, p, tq[1] * kBM, h, b);
       bool ok = true;
       int j = 0;
       for (; j < n_kv; ++j) {
@@ -172,64 +212,84 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0 && n_kv > 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(kBM, HD, false, true);
-      const uint32_t q_addr = smem_u32(sQ);
       bool ok = mbar_wait(&q_full, 0, &abort_flag, p.wait_limit_ns);
       if (!ok) report_error(kDevWaitTimeout, kid * 256 + kSiteQ);
-      // iteration j: O += P_{j-1} V_{j-1} (j > 0), then S_j = Q K_j^T (j < n_kv)
-      for (int j = 0; j <= n_kv && ok; ++j) {
-        if (j > 0) {
-          if (!mbar_wait(&p_full, (j - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+      int kv_ready = -1;  // highest KV tile whose kv_full was waited for
+      auto wait_kv = [&](int j) -> bool {
+        if (j <= kv_ready) return true;
+        if (!mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, &abort_flag, p.wait_limit_ns)) {
+          report_error(kDevWaitTimeout, kid * 256 + kSiteKV);
+          return false;
+        }
+        kv_ready = j;
+        return true;
+      };
+      auto issue_s = [&](int g, int j) {
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + g * C::TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sK + (j % kStages) * C::TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t dq = smem_desc(q_addr + kk * 32, 16, C::SBO, C::LAYOUT);
+          const uint64_t dk = smem_desc(k_addr + kk * 32, 16, C::SBO, C::LAYOUT);
+          mma_f16_ss(tmem_base + g * kBN, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&s_full[g]);
+      };
+      if (ok) ok = wait_kv(0);
+      if (ok) {
+        for (int g = 0; g < 2; ++g)
+          if (last[g] > 0) issue_s(g, 0);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        for (int g = 0; g < 2 && ok; ++g) {
+          if (j >= last[g]) continue;
+          if (!mbar_wait(&p_full[g], j & 1, &abort_flag, p.wait_limit_ns)) {
             report_error(kDevWaitTimeout, kid * 256 + kSiteP);
             ok = false;
             break;
           }
           tc_fence_after();
-          const int sp = (j - 1) % kStages;
-          const uint32_t v_addr = smem_u32(sV + sp * C::TILE_BYTES);
+          const uint32_t v_addr = smem_u32(sV + (j % kStages) * C::TILE_BYTES);
 #pragma unroll
           for (int ks = 0; ks < kBN / 16; ++ks) {
             const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
-            mma_f16_ts(tmem_base + kColO, tmem_base + ks * 8, dv, idesc_o, (j > 1 || ks > 0) ? 1u : 0u);
+            mma_f16_ts(tmem_base + kColO + g * 128, tmem_base + g * kBN + ks * 8, dv, idesc_o,
+                       (j > 0 || ks > 0) ? 1u : 0u);
           }
-          mma_commit(&kv_empty[sp]);
-          if (j == n_kv) mma_commit(&o_full);
-        }
-        if (j < n_kv) {
-          const int s = j % kStages;
-          if (!mbar_wait(&kv_full[s], (j / kStages) & 1, &abort_flag, p.wait_limit_ns)) {
-            report_error(kDevWaitTimeout, kid * 256 + kSiteKV);
-            ok = false;
-            break;
+          // the last reader of K_j / V_j releases the stage
+          if (g == 1 || j >= last[1]) mma_commit(&kv_empty[j % kStages]);
+          if (j + 1 < last[g]) {
+            if (!wait_kv(j + 1)) {
+              ok = false;
+              break;
+            }
+            issue_s(g, j + 1);
           }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(sK + s * C::TILE_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t dq = smem_desc(q_addr + kk * 32, 16, C::SBO, C::LAYOUT);
-            const uint64_t dk = smem_desc(k_addr + kk * 32, 16, C::SBO, C::LAYOUT);
-            mma_f16_ss(tmem_base, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full);
         }
       }
+      mma_commit(&o_full);  // every MMA issued so far (all of them on success)
       if (!ok) {
         abort_flag = 1;
-        mma_commit(&o_full);  // completes once every MMA issued so far is done
         mbar_wait(&o_full, 0, nullptr, kDrainLimitNs);
       }
     }
     __syncwarp();
   } else {
-    // ---------------- softmax (one query row per thread) ----------------
+    // ---------------- softmax, group g, one query row per thread ----------------
+    const int g = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + static_cast<int>(lane);
-    const int q_idx = qt * kBM + r;
+    const int q_idx = tq[g] * kBM + r;
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t t_s = t_lane + g * kBN;
+    const uint32_t t_o = t_lane + kColO + g * 128;
+    const float sl = p.scale_log2;
     float m = -INFINITY;  // running max, raw score units
     float l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&s_full, j & 1, &abort_flag, p.wait_limit_ns)) {
+    for (int j = 0; j < last[g]; ++j) {
+      if (!mbar_wait(&s_full[g], j & 1, &abort_flag, p.wait_limit_ns)) {
         report_error(kDevWaitTimeout, kid * 256 + kSiteS);
         abort_flag = 1;
         ok = false;
@@ -242,22 +302,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (p.causal) lim = min(lim, q_idx - k0 + 1);
       lim = max(0, min(kBN, lim));
 
-      // The whole 128-column score row in registers: one TMEM round trip.
+      // the whole 128-column score row in registers: one TMEM round trip
       uint32_t sv[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(t_lane + c * 32, sv[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sv[c]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);  // first waits, the rest only pin registers
-      // Masking is only needed on the causal diagonal tile and the tile
-      // holding the kv bound; `full` is warp-uniform elsewhere.
+      for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);  // the first waits, the rest pin registers
+      // masking only on the causal diagonal / kv-bound tile; warp-uniform elsewhere
       const bool full = lim >= kBN;
-      // row max with four independent chains
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (full) {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; ++t) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
+          for (int t = 0; t < 32; t += 2)
+            mx4[(t >> 1) & 3] = max3(mx4[(t >> 1) & 3], __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]));
       } else {
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -269,69 +328,72 @@ __global__ void __launch_bounds__(kThreads, 2)
       float m_use = m;
       float alpha = 1.f;
       if (mx > m) {
-        if (m == -INFINITY || (mx - m) * p.scale_log2 > kLazyRescaleLog2) {
-          alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - mx) * p.scale_log2);
+        if (m == -INFINITY || (mx - m) * sl > kLazyRescaleLog2) {
+          alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - mx) * sl);
           m_use = mx;
         }
       }
-      const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * p.scale_log2;
-      // P = 2^(s*c - m*c), packed fp16 pairs over S columns [0, 64); the
+      const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
+      // P = 2^(s*c - m*c), packed fp16 pairs over S_g columns [0, 64); the
       // columns written for chunk c were all read into registers above.
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int t = 0; t < 32; t += 2) {
-          float p0 = ex2_approx(fmaf(__uint_as_float(sv[c][t]), p.scale_log2, neg_mc));
-          float p1 = ex2_approx(fmaf(__uint_as_float(sv[c][t + 1]), p.scale_log2, neg_mc));
+          float x0, x1;
+          fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
+          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
           if (!full) {
             p0 = (c * 32 + t < lim) ? p0 : 0.f;
             p1 = (c * 32 + t + 1 < lim) ? p1 : 0.f;
           }
-          rs4[(t >> 1) & 3] += p0 + p1;
+          const int a = ((t >> 1) & 3) * 2;
+          add2(rs[a], rs[a + 1], p0, p1);
           pk[t / 2] = pack_half2(p0, p1);
         }
-        tmem_st16(t_lane + c * 16, pk);
+        tmem_st16(t_s + c * 16, pk);
       }
-      const float rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
-      // O rescale: S_j's completion implies PV_{j-1} (issued before it) is done.
+      const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+      // O rescale: S_g(j)'s completion implies PV_g(j-1) (issued before it) is done.
       const bool need = (j > 0) && (alpha != 1.f);
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
         for (int c = 0; c < HD; c += 16) {
           uint32_t o[16];
-          tmem_ld16(t_lane + kColO + c, o);
+          tmem_ld16(t_o + c, o);
           tmem_ld_wait(o);
 #pragma unroll
           for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-          tmem_st16(t_lane + kColO + c, o);
+          tmem_st16(t_o + c, o);
         }
       }
-      l = l * alpha + rs;
+      l = l * alpha + row_sum;
       m = m_use;
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full);
+      if (lane == 0) mbar_arrive(&p_full[g]);
     }
     // epilogue: O / l -> fp16 [b, q, h*HD + c]
-    if (ok && n_kv > 0) {
+    const bool tile_ok = tq[g] < q_tiles;
+    if (ok && last[g] > 0) {
       if (!mbar_wait(&o_full, 0, &abort_flag, p.wait_limit_ns)) {
         report_error(kDevWaitTimeout, kid * 256 + kSiteO);
         abort_flag = 1;
         ok = false;
       }
     }
-    if (ok) {
+    if (ok && tile_ok) {
       tc_fence_after();
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       __half* dst = p.out + (static_cast<int64_t>(b) * p.S + q_idx) * p.ld_out + h * HD;
 #pragma unroll
       for (int c = 0; c < HD; c += 16) {
         uint32_t o[16];
-        if (n_kv > 0) {
-          tmem_ld16(t_lane + kColO + c, o);
+        if (last[g] > 0) {
+          tmem_ld16(t_o + c, o);
           tmem_ld_wait(o);
         } else {
 #pragma unroll
