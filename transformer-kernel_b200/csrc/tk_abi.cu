@@ -388,7 +388,9 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
   p.heads_inner = heads_inner ? 1 : 0;
   p.wait_limit_ns = g_wait_limit_ns.load();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned grid = static_cast<unsigned>(B * H * ((q_tiles + 1) / 2));  // one CTA per pair of query tiles
+  // persistent: one CTA per SM over the (b, h, query-tile pair) work items
+  const int64_t items = B * H * ((q_tiles + 1) / 2);
+  const unsigned grid = static_cast<unsigned>(items < info->sms ? items : info->sms);
   cudaError_t e;
   if (hd == 64) {
     auto kern = tk::attn::attn_fwd_kernel<64>;

@@ -17,7 +17,10 @@
 // projection (head stride hd < row stride 3d), {hd, S, H, B} for [B,H,S,hd]
 // contiguous tensors.
 //
-// One CTA per (b, h, pair of 128-query tiles), one CTA per SM. Warp roles:
+// Persistent: one CTA per SM loops over work items (b, h, pair of 128-query
+// tiles), heaviest first; TMEM stays allocated, Q is double-buffered, the
+// K/V ring and all barrier phases run on across items, and the next item's
+// first S = QK^T overlaps the current item's epilogue. Warp roles:
 // warp 0 TMA, warp 1 TMEM owner + MMA issuer, warps 2..5 softmax group 0
 // (query tile 2p), warps 6..9 softmax group 1 (tile 2p+1); each softmax
 // thread owns one query row (its warp's TMEM lane quadrant). Both groups
@@ -81,7 +84,7 @@ struct Cfg {
   static constexpr SmemLayout LAYOUT = HD == 64 ? kLayoutSW128 : kLayoutSW64;
   static constexpr int TILE_BYTES = kBM * ROW_BYTES;           // Q, K or V tile
   static constexpr int SBO = 8 * ROW_BYTES;                    // 8-row core-matrix group
-  static constexpr int SMEM_BYTES = TILE_BYTES * (2 + 2 * kStages) + 1024;
+  static constexpr int SMEM_BYTES = TILE_BYTES * (4 + 2 * kStages) + 1024;  // 2 Q sets of 2 tiles
 };
 
 // ---- packed fp32 helpers (sm_100 f32x2 FMA/ADD, 3-input max) ----
@@ -110,51 +113,72 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
-enum : unsigned { kSiteQ = 1, kSiteKV = 2, kSiteS = 3, kSiteP = 4, kSiteO = 5, kSiteEmpty = 6, kSiteDrain = 7 };
+enum : unsigned { kSiteQ = 1, kSiteKV = 2, kSiteS = 3, kSiteP = 4, kSiteO = 5, kSiteEmpty = 6, kSiteOFree = 7,
+                  kSiteQEmpty = 8 };
+
+// One work item = (b, h, pair of query tiles); heaviest (last, for causal)
+// pairs first so the static round-robin over CTAs stays balanced.
+struct Item {
+  int b, h, tq0, tq1, kv_bound;
+  int last[2];  // KV tiles attended by group 0 / group 1 (0 = group idle)
+  int n_kv;
+  bool has1;
+};
+
+__device__ __forceinline__ Item make_item(const Params& p, int idx, int q_tiles, int q_pairs) {
+  Item it;
+  const int bh_count = p.B * p.H;
+  const int qp = q_pairs - 1 - idx / bh_count;
+  const int bh = idx % bh_count;
+  it.b = bh / p.H;
+  it.h = bh % p.H;
+  it.tq0 = 2 * qp;
+  it.tq1 = 2 * qp + 1;
+  it.has1 = it.tq1 < q_tiles;
+  it.kv_bound = p.S;
+  if (p.kv_len != nullptr) it.kv_bound = max(0, min(p.S, p.kv_len[it.b]));
+  const int n_all = (it.kv_bound + kBN - 1) / kBN;
+  it.last[0] = p.causal ? min(n_all, it.tq0 + 1) : n_all;
+  it.last[1] = it.has1 ? (p.causal ? min(n_all, it.tq1 + 1) : n_all) : 0;
+  it.n_kv = max(it.last[0], it.last[1]);
+  return it;
+}
 
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(200)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, Params p) {
   using C = Cfg<HD>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full;
+  __shared__ __align__(8) uint64_t q_full[2];      // per Q buffer set
+  __shared__ __align__(8) uint64_t q_empty[2];
   __shared__ __align__(8) uint64_t kv_full[kStages];
   __shared__ __align__(8) uint64_t kv_empty[kStages];
-  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t s_full[2];      // per softmax group
   __shared__ __align__(8) uint64_t p_full[2];
-  __shared__ __align__(8) uint64_t o_full;
+  __shared__ __align__(8) uint64_t o_full[2];
+  __shared__ __align__(8) uint64_t o_free[2];
+  __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                   // 2 tiles
-  uint8_t* sK = smem + 2 * C::TILE_BYTES;               // kStages tiles
-  uint8_t* sV = smem + C::TILE_BYTES * (2 + kStages);   // kStages tiles
+  uint8_t* sQ = smem;                                   // 2 sets x 2 tiles
+  uint8_t* sK = smem + 4 * C::TILE_BYTES;               // kStages tiles
+  uint8_t* sV = smem + C::TILE_BYTES * (4 + kStages);   // kStages tiles
 
   const int warp = warp_id_uniform();
   const uint32_t lane = lane_id();
   const int q_tiles = (p.S + kBM - 1) / kBM;
   const int q_pairs = (q_tiles + 1) / 2;
-  const int bh_count = p.B * p.H;
-  // Heaviest (last, for causal) tile pairs are launched first.
-  const int qp = q_pairs - 1 - static_cast<int>(blockIdx.x / bh_count);
-  const int bh = static_cast<int>(blockIdx.x % bh_count);
-  const int b = bh / p.H, h = bh % p.H;
-  const int tq[2] = {2 * qp, 2 * qp + 1};
-  const bool has1 = tq[1] < q_tiles;
-  int kv_bound = p.S;
-  if (p.kv_len != nullptr) kv_bound = max(0, min(p.S, p.kv_len[b]));
-  const int n_all = (kv_bound + kBN - 1) / kBN;
-  // number of KV tiles each group attends to
-  int last[2];
-  last[0] = p.causal ? min(n_all, tq[0] + 1) : n_all;
-  last[1] = has1 ? (p.causal ? min(n_all, tq[1] + 1) : n_all) : 0;
-  const int n_kv = max(last[0], last[1]);
+  const int n_items = q_pairs * p.B * p.H;
   const unsigned kid = 0x80u + HD;
 
   if (threadIdx.x == 0) {
-    mbar_init(&q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -162,8 +186,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int g = 0; g < 2; ++g) {
       mbar_init(&s_full[g], 1);
       mbar_init(&p_full[g], 4);
+      mbar_init(&o_full[g], 1);
+      mbar_init(&o_free[g], 4);
     }
-    mbar_init(&o_full, 1);
+    mbar_init(&drain_bar, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -178,101 +204,144 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0) {
       prefetch_tensormap(&map_q);
       prefetch_tensormap(&map_k);
       prefetch_tensormap(&map_v);
-      mbar_arrive_expect_tx(&q_full, C::TILE_BYTES * (has1 ? 2 : 1));
-      load_tile(sQ, &map_q, &q_full, p, tq[0] * kBM, h, b);
-      if (has1) load_tile(sQ + C::TILE_BYTES, &map_q, &q_full, p, tq[1] * kBM, h, b);
+      int kv_count = 0;  // KV tiles loaded so far (ring position)
+      int qn = 0;        // items with work loaded so far (Q buffer set = qn & 1)
       bool ok = true;
-      int j = 0;
-      for (; j < n_kv; ++j) {
-        const int s = j % kStages;
-        const uint32_t ph = (j / kStages) & 1;
-        if (!mbar_wait(&kv_empty[s], ph ^ 1u, &abort_flag, p.wait_limit_ns)) {
-          report_error(kDevWaitTimeout, kid * 256 + kSiteEmpty);
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+        const Item it = make_item(p, idx, q_tiles, q_pairs);
+        if (it.n_kv == 0) continue;
+        const int qs = qn & 1;
+        const uint32_t q_phase = (qn >> 1) & 1;
+        ++qn;
+        if (!mbar_wait(&q_empty[qs], q_phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
+          report_error(kDevWaitTimeout, kid * 256 + kSiteQEmpty);
           abort_flag = 1;
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[s], 2 * C::TILE_BYTES);
-        load_tile(sK + s * C::TILE_BYTES, &map_k, &kv_full[s], p, j * kBN, h, b);
-        load_tile(sV + s * C::TILE_BYTES, &map_v, &kv_full[s], p, j * kBN, h, b);
+        uint8_t* q_dst = sQ + qs * 2 * C::TILE_BYTES;
+        mbar_arrive_expect_tx(&q_full[qs], C::TILE_BYTES * (it.has1 ? 2 : 1));
+        load_tile(q_dst, &map_q, &q_full[qs], p, it.tq0 * kBM, it.h, it.b);
+        if (it.has1) load_tile(q_dst + C::TILE_BYTES, &map_q, &q_full[qs], p, it.tq1 * kBM, it.h, it.b);
+        for (int j = 0; j < it.n_kv; ++j, ++kv_count) {
+          const int s = kv_count % kStages;
+          const uint32_t ph = (kv_count / kStages) & 1;
+          if (!mbar_wait(&kv_empty[s], ph ^ 1u, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteEmpty);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[s], 2 * C::TILE_BYTES);
+          load_tile(sK + s * C::TILE_BYTES, &map_k, &kv_full[s], p, j * kBN, it.h, it.b);
+          load_tile(sV + s * C::TILE_BYTES, &map_v, &kv_full[s], p, j * kBN, it.h, it.b);
+        }
       }
       if (!ok) {
-        mbar_wait(&q_full, 0, nullptr, kDrainLimitNs);
-        for (int t = max(0, j - kStages); t < j; ++t)
+        // let copies already in flight land before the CTA can exit
+        for (int t = max(0, kv_count - kStages); t < kv_count; ++t)
           mbar_wait(&kv_full[t % kStages], (t / kStages) & 1, nullptr, kDrainLimitNs);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0 && n_kv > 0) {
+    if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(kBM, HD, false, true);
-      bool ok = mbar_wait(&q_full, 0, &abort_flag, p.wait_limit_ns);
-      if (!ok) report_error(kDevWaitTimeout, kid * 256 + kSiteQ);
-      int kv_ready = -1;  // highest KV tile whose kv_full was waited for
-      auto wait_kv = [&](int j) -> bool {
-        if (j <= kv_ready) return true;
-        if (!mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, &abort_flag, p.wait_limit_ns)) {
-          report_error(kDevWaitTimeout, kid * 256 + kSiteKV);
-          return false;
-        }
-        kv_ready = j;
-        return true;
+      int kv_count = 0;          // KV tiles consumed so far (ring position)
+      int tiles_g[2] = {0, 0};   // tiles processed by each group (s_full / p_full phases)
+      int o_uses[2] = {0, 0};    // items in which each group accumulated O (o_full / o_free phases)
+      int qn = 0;                // items with work consumed so far (Q buffer set = qn & 1)
+      bool ok = true;
+      auto fail = [&](unsigned site) {
+        report_error(kDevWaitTimeout, kid * 256 + site);
+        ok = false;
       };
-      auto issue_s = [&](int g, int j) {
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + g * C::TILE_BYTES);
-        const uint32_t k_addr = smem_u32(sK + (j % kStages) * C::TILE_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t dq = smem_desc(q_addr + kk * 32, 16, C::SBO, C::LAYOUT);
-          const uint64_t dk = smem_desc(k_addr + kk * 32, 16, C::SBO, C::LAYOUT);
-          mma_f16_ss(tmem_base + g * kBN, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
+      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+        const Item it = make_item(p, idx, q_tiles, q_pairs);
+        if (it.n_kv == 0) continue;
+        const int qs = qn & 1;
+        const uint32_t q_phase = (qn >> 1) & 1;
+        ++qn;
+        if (!mbar_wait(&q_full[qs], q_phase, &abort_flag, p.wait_limit_ns)) {
+          fail(kSiteQ);
+          break;
         }
-        mma_commit(&s_full[g]);
-      };
-      if (ok) ok = wait_kv(0);
-      if (ok) {
-        for (int g = 0; g < 2; ++g)
-          if (last[g] > 0) issue_s(g, 0);
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        for (int g = 0; g < 2 && ok; ++g) {
-          if (j >= last[g]) continue;
-          if (!mbar_wait(&p_full[g], j & 1, &abort_flag, p.wait_limit_ns)) {
-            report_error(kDevWaitTimeout, kid * 256 + kSiteP);
-            ok = false;
-            break;
+        const int kv_base = kv_count;
+        int kv_ready = -1;
+        auto wait_kv = [&](int j) -> bool {
+          if (j <= kv_ready) return true;
+          const int t = kv_base + j;
+          if (!mbar_wait(&kv_full[t % kStages], (t / kStages) & 1, &abort_flag, p.wait_limit_ns)) {
+            fail(kSiteKV);
+            return false;
           }
+          kv_ready = j;
+          return true;
+        };
+        auto issue_s = [&](int g, int j) {
           tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + (j % kStages) * C::TILE_BYTES);
+          const uint32_t q_addr = smem_u32(sQ + (qs * 2 + g) * C::TILE_BYTES);
+          const uint32_t k_addr = smem_u32(sK + ((kv_base + j) % kStages) * C::TILE_BYTES);
 #pragma unroll
-          for (int ks = 0; ks < kBN / 16; ++ks) {
-            const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
-            mma_f16_ts(tmem_base + kColO + g * 128, tmem_base + g * kBN + ks * 8, dv, idesc_o,
-                       (j > 0 || ks > 0) ? 1u : 0u);
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint64_t dq = smem_desc(q_addr + kk * 32, 16, C::SBO, C::LAYOUT);
+            const uint64_t dk = smem_desc(k_addr + kk * 32, 16, C::SBO, C::LAYOUT);
+            mma_f16_ss(tmem_base + g * kBN, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
           }
-          // the last reader of K_j / V_j releases the stage
-          if (g == 1 || j >= last[1]) mma_commit(&kv_empty[j % kStages]);
-          if (j + 1 < last[g]) {
-            if (!wait_kv(j + 1)) {
-              ok = false;
+          mma_commit(&s_full[g]);
+        };
+        if (!wait_kv(0)) break;
+        for (int g = 0; g < 2; ++g)
+          if (it.last[g] > 0) issue_s(g, 0);
+        for (int j = 0; j < it.n_kv && ok; ++j) {
+          for (int g = 0; g < 2 && ok; ++g) {
+            if (j >= it.last[g]) continue;
+            if (!mbar_wait(&p_full[g], tiles_g[g] & 1, &abort_flag, p.wait_limit_ns)) {
+              fail(kSiteP);
               break;
             }
-            issue_s(g, j + 1);
+            ++tiles_g[g];
+            if (j == 0 && o_uses[g] > 0) {
+              // the previous item's epilogue of group g must be done reading O_g
+              if (!mbar_wait(&o_free[g], (o_uses[g] - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+                fail(kSiteOFree);
+                break;
+              }
+            }
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(sV + ((kv_base + j) % kStages) * C::TILE_BYTES);
+#pragma unroll
+            for (int ks = 0; ks < kBN / 16; ++ks) {
+              const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
+              mma_f16_ts(tmem_base + kColO + g * 128, tmem_base + g * kBN + ks * 8, dv, idesc_o,
+                         (j > 0 || ks > 0) ? 1u : 0u);
+            }
+            // the last reader of K_j / V_j releases the stage
+            if (g == 1 || j >= it.last[1]) mma_commit(&kv_empty[(kv_base + j) % kStages]);
+            if (j + 1 == it.last[g]) {
+              mma_commit(&o_full[g]);
+              ++o_uses[g];
+            }
+            if (j + 1 < it.last[g]) {
+              if (!wait_kv(j + 1)) break;
+              issue_s(g, j + 1);
+            }
           }
         }
+        if (!ok) break;
+        mma_commit(&q_empty[qs]);  // every S of this item read its Q set
+        kv_count += it.n_kv;
       }
-      mma_commit(&o_full);  // every MMA issued so far (all of them on success)
-      if (!ok) {
-        abort_flag = 1;
-        mbar_wait(&o_full, 0, nullptr, kDrainLimitNs);
-      }
+      // everything issued is complete before TMEM can be released
+      mma_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, nullptr, ok ? p.wait_limit_ns : kDrainLimitNs);
+      if (!ok) abort_flag = 1;
     }
     __syncwarp();
   } else {
@@ -280,138 +349,151 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + static_cast<int>(lane);
-    const int q_idx = tq[g] * kBM + r;
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t t_s = t_lane + g * kBN;
     const uint32_t t_o = t_lane + kColO + g * 128;
     const float sl = p.scale_log2;
-    float m = -INFINITY;  // running max, raw score units
-    float l = 0.f;
+    int tiles = 0, o_uses = 0;
     bool ok = true;
-    for (int j = 0; j < last[g]; ++j) {
-      if (!mbar_wait(&s_full[g], j & 1, &abort_flag, p.wait_limit_ns)) {
-        report_error(kDevWaitTimeout, kid * 256 + kSiteS);
-        abort_flag = 1;
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int k0 = j * kBN;
-      // keys k0 + c are valid iff c < lim (causal diagonal and the kv bound)
-      int lim = kv_bound - k0;
-      if (p.causal) lim = min(lim, q_idx - k0 + 1);
-      lim = max(0, min(kBN, lim));
+    for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+      const Item it = make_item(p, idx, q_tiles, q_pairs);
+      const int tq = g == 0 ? it.tq0 : it.tq1;
+      const int n_g = it.last[g];
+      const int q_idx = tq * kBM + r;
+      float m = -INFINITY;  // running max, raw score units
+      float l = 0.f;
+      for (int j = 0; j < n_g; ++j, ++tiles) {
+        if (!mbar_wait(&s_full[g], tiles & 1, &abort_flag, p.wait_limit_ns)) {
+          report_error(kDevWaitTimeout, kid * 256 + kSiteS);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int k0 = j * kBN;
+        // keys k0 + c are valid iff c < lim (causal diagonal and the kv bound)
+        int lim = it.kv_bound - k0;
+        if (p.causal) lim = min(lim, q_idx - k0 + 1);
+        lim = max(0, min(kBN, lim));
 
-      // the whole 128-column score row in registers: one TMEM round trip
-      uint32_t sv[4][32];
+        // the whole 128-column score row in registers: one TMEM round trip
+        uint32_t sv[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sv[c]);
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sv[c]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);  // the first waits, the rest pin registers
-      // masking only on the causal diagonal / kv-bound tile; warp-uniform elsewhere
-      const bool full = lim >= kBN;
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (full) {
+        for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);  // the first waits, the rest pin registers
+        // masking only on the causal diagonal / kv-bound tile; warp-uniform elsewhere
+        const bool full = lim >= kBN;
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (full) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; t += 2)
-            mx4[(t >> 1) & 3] = max3(mx4[(t >> 1) & 3], __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]));
-      } else {
+            for (int t = 0; t < 32; t += 2)
+              mx4[(t >> 1) & 3] = max3(mx4[(t >> 1) & 3], __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]));
+        } else {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; ++t)
-            if (c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
-      }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      float m_use = m;
-      float alpha = 1.f;
-      if (mx > m) {
-        if (m == -INFINITY || (mx - m) * sl > kLazyRescaleLog2) {
-          alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - mx) * sl);
-          m_use = mx;
+            for (int t = 0; t < 32; ++t)
+              if (c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
         }
-      }
-      const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
-      // P = 2^(s*c - m*c), packed fp16 pairs over S_g columns [0, 64); the
-      // columns written for chunk c were all read into registers above.
-      float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int t = 0; t < 32; t += 2) {
-          float x0, x1;
-          fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
-          float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-          if (!full) {
-            p0 = (c * 32 + t < lim) ? p0 : 0.f;
-            p1 = (c * 32 + t + 1 < lim) ? p1 : 0.f;
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        float m_use = m;
+        float alpha = 1.f;
+        if (mx > m) {
+          if (m == -INFINITY || (mx - m) * sl > kLazyRescaleLog2) {
+            alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - mx) * sl);
+            m_use = mx;
           }
-          const int a = ((t >> 1) & 3) * 2;
-          add2(rs[a], rs[a + 1], p0, p1);
-          pk[t / 2] = pack_half2(p0, p1);
         }
-        tmem_st16(t_s + c * 16, pk);
+        const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
+        // P = 2^(s*c - m*c), packed fp16 pairs over S_g columns [0, 64); the
+        // columns written for chunk c were all read into registers above.
+        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            float x0, x1;
+            fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
+            float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+            if (!full) {
+              p0 = (c * 32 + t < lim) ? p0 : 0.f;
+              p1 = (c * 32 + t + 1 < lim) ? p1 : 0.f;
+            }
+            const int a = ((t >> 1) & 3) * 2;
+            add2(rs[a], rs[a + 1], p0, p1);
+            pk[t / 2] = pack_half2(p0, p1);
+          }
+          tmem_st16(t_s + c * 16, pk);
+        }
+        const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+        // O rescale: S_g(j)'s completion implies PV_g(j-1) (issued before it) is done.
+        const bool need = (j > 0) && (alpha != 1.f);
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < HD; c += 16) {
+            uint32_t o[16];
+            tmem_ld16(t_o + c, o);
+            tmem_ld_wait(o);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+            tmem_st16(t_o + c, o);
+          }
+        }
+        l = l * alpha + row_sum;
+        m = m_use;
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[g]);
       }
-      const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
-      // O rescale: S_g(j)'s completion implies PV_g(j-1) (issued before it) is done.
-      const bool need = (j > 0) && (alpha != 1.f);
-      if (__any_sync(0xffffffffu, need)) {
+      if (!ok) break;
+      // epilogue: O / l -> fp16 [b, q, h*HD + c]
+      if (n_g > 0) {
+        if (!mbar_wait(&o_full[g], o_uses & 1, &abort_flag, p.wait_limit_ns)) {
+          report_error(kDevWaitTimeout, kid * 256 + kSiteO);
+          abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (tq < q_tiles) {
+        const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+        __half* dst = p.out + (static_cast<int64_t>(it.b) * p.S + q_idx) * p.ld_out + it.h * HD;
 #pragma unroll
         for (int c = 0; c < HD; c += 16) {
           uint32_t o[16];
-          tmem_ld16(t_o + c, o);
-          tmem_ld_wait(o);
+          if (n_g > 0) {
+            tmem_ld16(t_o + c, o);
+            tmem_ld_wait(o);
+          } else {
 #pragma unroll
-          for (int t = 0; t < 16; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
-          tmem_st16(t_o + c, o);
+            for (int t = 0; t < 16; ++t) o[t] = 0u;
+          }
+          if (q_idx < p.S) {
+            uint4 w0, w1;
+            w0.x = pack_half2(__uint_as_float(o[0]) * inv_l, __uint_as_float(o[1]) * inv_l);
+            w0.y = pack_half2(__uint_as_float(o[2]) * inv_l, __uint_as_float(o[3]) * inv_l);
+            w0.z = pack_half2(__uint_as_float(o[4]) * inv_l, __uint_as_float(o[5]) * inv_l);
+            w0.w = pack_half2(__uint_as_float(o[6]) * inv_l, __uint_as_float(o[7]) * inv_l);
+            w1.x = pack_half2(__uint_as_float(o[8]) * inv_l, __uint_as_float(o[9]) * inv_l);
+            w1.y = pack_half2(__uint_as_float(o[10]) * inv_l, __uint_as_float(o[11]) * inv_l);
+            w1.z = pack_half2(__uint_as_float(o[12]) * inv_l, __uint_as_float(o[13]) * inv_l);
+            w1.w = pack_half2(__uint_as_float(o[14]) * inv_l, __uint_as_float(o[15]) * inv_l);
+            reinterpret_cast<uint4*>(dst + c)[0] = w0;
+            reinterpret_cast<uint4*>(dst + c)[1] = w1;
+          }
         }
       }
-      l = l * alpha + row_sum;
-      m = m_use;
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[g]);
-    }
-    // epilogue: O / l -> fp16 [b, q, h*HD + c]
-    const bool tile_ok = tq[g] < q_tiles;
-    if (ok && last[g] > 0) {
-      if (!mbar_wait(&o_full, 0, &abort_flag, p.wait_limit_ns)) {
-        report_error(kDevWaitTimeout, kid * 256 + kSiteO);
-        abort_flag = 1;
-        ok = false;
-      }
-    }
-    if (ok && tile_ok) {
-      tc_fence_after();
-      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
-      __half* dst = p.out + (static_cast<int64_t>(b) * p.S + q_idx) * p.ld_out + h * HD;
-#pragma unroll
-      for (int c = 0; c < HD; c += 16) {
-        uint32_t o[16];
-        if (last[g] > 0) {
-          tmem_ld16(t_o + c, o);
-          tmem_ld_wait(o);
-        } else {
-#pragma unroll
-          for (int t = 0; t < 16; ++t) o[t] = 0u;
-        }
-        if (q_idx < p.S) {
-          uint4 w0, w1;
-          w0.x = pack_half2(__uint_as_float(o[0]) * inv_l, __uint_as_float(o[1]) * inv_l);
-          w0.y = pack_half2(__uint_as_float(o[2]) * inv_l, __uint_as_float(o[3]) * inv_l);
-          w0.z = pack_half2(__uint_as_float(o[4]) * inv_l, __uint_as_float(o[5]) * inv_l);
-          w0.w = pack_half2(__uint_as_float(o[6]) * inv_l, __uint_as_float(o[7]) * inv_l);
-          w1.x = pack_half2(__uint_as_float(o[8]) * inv_l, __uint_as_float(o[9]) * inv_l);
-          w1.y = pack_half2(__uint_as_float(o[10]) * inv_l, __uint_as_float(o[11]) * inv_l);
-          w1.z = pack_half2(__uint_as_float(o[12]) * inv_l, __uint_as_float(o[13]) * inv_l);
-          w1.w = pack_half2(__uint_as_float(o[14]) * inv_l, __uint_as_float(o[15]) * inv_l);
-          reinterpret_cast<uint4*>(dst + c)[0] = w0;
-          reinterpret_cast<uint4*>(dst + c)[1] = w1;
-        }
+      if (n_g > 0) {
+        ++o_uses;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[g]);
       }
     }
   }
