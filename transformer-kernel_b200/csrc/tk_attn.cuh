@@ -145,7 +145,7 @@ __device__ __forceinline__ Item make_item(const Params& p, int idx, int q_tiles,
 }
 
 template <int HD>
-__global__ void __maxnreg__(184)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v, Params p) {
   using C = Cfg<HD>;
