@@ -25,15 +25,15 @@
 // (query tile 2p), warps 6..9 softmax group 1 (tile 2p+1); each softmax
 // thread owns one query row (its warp's TMEM lane quadrant). Both groups
 // share every K/V tile. TMEM (512 columns): S_g = Q_g K^T in columns
-// [128g, 128g+128) fp32, P_g = softmax numerators as packed fp16 pairs over
-// S_g columns [128g, 128g+64), O_g in columns [256+128g, 256+128g+HD).
+// [128g, 128g+128) fp32, P_g = softmax numerators as packed fp16 pairs in
+// [256+64g, 320+64g), O_g in [384+64g, 384+64g+HD).
 //   S_g(j) : tcgen05.mma SS, M=128 N=128 K=16 x (HD/16)     (A=Q_g, B=K_j, both K-major)
 //   O_g   += P_g(j) V_j : tcgen05.mma TS, M=128 N=HD K=16 x 8 (A=P_g in TMEM, B=V_j MN-major)
-// The MMA warp issues S0(0) S1(0) | PV0(0) S0(1) | PV1(0) S1(1) | PV0(1) ...
-// so one group's softmax runs while the tensor core works for the other.
-// tcgen05.mma from one thread execute in order: S_g(j+1) (which overwrites
-// P_g(j)) follows PV_g(j), and the completion of S_g(j+1) tells group g that
-// PV_g(j) has finished with O_g.
+// As soon as group g hands over P_g(j), the MMA warp issues S_g(j+1) and
+// then PV_g(j): the next scores are ready while PV runs, and group g waits
+// for PV_g(j) (pv_done) only right before it overwrites P_g or rescales O_g.
+// With two groups, one group's softmax runs while the tensor core works for
+// the other.
 //
 // Online softmax keeps the running max m in raw-score units and rescales
 // O and l only when the max grows by more than 2^8 in the exponent (lazy
@@ -54,7 +54,8 @@ constexpr int kBN = 128;  // keys per KV tile
 constexpr int kThreads = 320;
 constexpr int kStages = 4;
 constexpr int kTmemCols = 512;
-constexpr int kColO = 256;
+constexpr int kColP = 256;  // P_g at kColP + 64 g (packed fp16 pairs)
+constexpr int kColO = 384;  // O_g at kColO + 64 g (fp32, HD <= 64 columns)
 constexpr float kLazyRescaleLog2 = 8.f;
 
 struct Params {
@@ -114,7 +115,7 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 }
 
 enum : unsigned { kSiteQ = 1, kSiteKV = 2, kSiteS = 3, kSiteP = 4, kSiteO = 5, kSiteEmpty = 6, kSiteOFree = 7,
-                  kSiteQEmpty = 8 };
+                  kSiteQEmpty = 8, kSitePv = 9 };
 
 // One work item = (b, h, pair of query tiles); heaviest (last, for causal)
 // pairs first so the static round-robin over CTAs stays balanced.
@@ -158,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t p_full[2];
   __shared__ __align__(8) uint64_t o_full[2];
   __shared__ __align__(8) uint64_t o_free[2];
+  __shared__ __align__(8) uint64_t pv_done[2];
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -188,6 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_full[g], 4);
       mbar_init(&o_full[g], 1);
       mbar_init(&o_free[g], 4);
+      mbar_init(&pv_done[g], 1);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -307,6 +310,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             ++tiles_g[g];
+            // S_g(j+1) first: it overwrites S_g, which the softmax has finished
+            // reading; P_g(j) lives in its own columns, so PV_g(j) can follow.
+            if (j + 1 < it.last[g]) {
+              if (!wait_kv(j + 1)) break;
+              issue_s(g, j + 1);
+            }
             if (j == 0 && o_uses[g] > 0) {
               // the previous item's epilogue of group g must be done reading O_g
               if (!mbar_wait(&o_free[g], (o_uses[g] - 1) & 1, &abort_flag, p.wait_limit_ns)) {
@@ -319,18 +328,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int ks = 0; ks < kBN / 16; ++ks) {
               const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
-              mma_f16_ts(tmem_base + kColO + g * 128, tmem_base + g * kBN + ks * 8, dv, idesc_o,
+              mma_f16_ts(tmem_base + kColO + g * 64, tmem_base + kColP + g * 64 + ks * 8, dv, idesc_o,
                          (j > 0 || ks > 0) ? 1u : 0u);
             }
+            mma_commit(&pv_done[g]);  // P_g and O_g free for the softmax of tile j+1
             // the last reader of K_j / V_j releases the stage
             if (g == 1 || j >= it.last[1]) mma_commit(&kv_empty[(kv_base + j) % kStages]);
             if (j + 1 == it.last[g]) {
               mma_commit(&o_full[g]);
               ++o_uses[g];
-            }
-            if (j + 1 < it.last[g]) {
-              if (!wait_kv(j + 1)) break;
-              issue_s(g, j + 1);
             }
           }
         }
@@ -351,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quad * 32 + static_cast<int>(lane);
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t t_s = t_lane + g * kBN;
-    const uint32_t t_o = t_lane + kColO + g * 128;
+    const uint32_t t_p = t_lane + kColP + g * 64;
+    const uint32_t t_o = t_lane + kColO + g * 64;
     const float sl = p.scale_log2;
     int tiles = 0, o_uses = 0;
     bool ok = true;
@@ -408,29 +415,53 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
-        // P = 2^(s*c - m*c), packed fp16 pairs over S_g columns [0, 64); the
-        // columns written for chunk c were all read into registers above.
-        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // P = 2^(s*c - m*c) in independent passes (all exponents, then all
+        // ex2 back to back on the SFU, then sums and fp16 packing), in place.
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int t = 0; t < 32; t += 2) {
             float x0, x1;
             fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
-            float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
-            if (!full) {
-              p0 = (c * 32 + t < lim) ? p0 : 0.f;
-              p1 = (c * 32 + t + 1 < lim) ? p1 : 0.f;
-            }
+            sv[c][t] = __float_as_uint(x0);
+            sv[c][t + 1] = __float_as_uint(x1);
+          }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; ++t) sv[c][t] = __float_as_uint(ex2_approx(__uint_as_float(sv[c][t])));
+        if (!full) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+              if (c * 32 + t >= lim) sv[c][t] = 0u;
+        }
+        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[4][16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            const float p0 = __uint_as_float(sv[c][t]), p1 = __uint_as_float(sv[c][t + 1]);
             const int a = ((t >> 1) & 3) * 2;
             add2(rs[a], rs[a + 1], p0, p1);
-            pk[t / 2] = pack_half2(p0, p1);
+            pk[c][t / 2] = pack_half2(p0, p1);
           }
-          tmem_st16(t_s + c * 16, pk);
-        }
         const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
-        // O rescale: S_g(j)'s completion implies PV_g(j-1) (issued before it) is done.
+        // PV_g of the previous tile (issued after S_g(j)) reads P_g and writes
+        // O_g: it must be complete before P_g is overwritten or O_g rescaled.
+        if (tiles > 0) {
+          if (!mbar_wait(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSitePv);
+            abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_st16(t_p + c * 16, pk[c]);
         const bool need = (j > 0) && (alpha != 1.f);
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
