@@ -29,9 +29,10 @@
 // [256+64g, 320+64g), O_g in [384+64g, 384+64g+HD).
 //   S_g(j) : tcgen05.mma SS, M=128 N=128 K=16 x (HD/16)     (A=Q_g, B=K_j, both K-major)
 //   O_g   += P_g(j) V_j : tcgen05.mma TS, M=128 N=HD K=16 x 8 (A=P_g in TMEM, B=V_j MN-major)
-// As soon as group g hands over P_g(j), the MMA warp issues S_g(j+1) and
-// then PV_g(j): the next scores are ready while PV runs, and group g waits
-// for PV_g(j) (pv_done) only right before it overwrites P_g or rescales O_g.
+// Group g signals s_free as soon as it has pulled S_g(j) into registers; the
+// MMA warp then computes S_g(j+1) during tile j's exponentials, and issues
+// PV_g(j) once P_g(j) is written (p_full). Group g waits for PV_g(j)
+// (pv_done) only right before it overwrites P_g or rescales O_g.
 // With two groups, one group's softmax runs while the tensor core works for
 // the other.
 //
@@ -115,7 +116,7 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 }
 
 enum : unsigned { kSiteQ = 1, kSiteKV = 2, kSiteS = 3, kSiteP = 4, kSiteO = 5, kSiteEmpty = 6, kSiteOFree = 7,
-                  kSiteQEmpty = 8, kSitePv = 9 };
+                  kSiteQEmpty = 8, kSitePv = 9, kSiteSFree = 10 };
 
 // One work item = (b, h, pair of query tiles); heaviest (last, for causal)
 // pairs first so the static round-robin over CTAs stays balanced.
@@ -160,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t o_full[2];
   __shared__ __align__(8) uint64_t o_free[2];
   __shared__ __align__(8) uint64_t pv_done[2];
+  __shared__ __align__(8) uint64_t s_free[2];
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&o_full[g], 1);
       mbar_init(&o_free[g], 4);
       mbar_init(&pv_done[g], 1);
+      mbar_init(&s_free[g], 4);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -259,6 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kv_count = 0;          // KV tiles consumed so far (ring position)
       int tiles_g[2] = {0, 0};   // tiles processed by each group (s_full / p_full phases)
       int o_uses[2] = {0, 0};    // items in which each group accumulated O (o_full / o_free phases)
+      int s_issued[2] = {0, 0};  // S_g MMAs issued (s_free phases)
       int qn = 0;                // items with work consumed so far (Q buffer set = qn & 1)
       bool ok = true;
       auto fail = [&](unsigned site) {
@@ -287,7 +291,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           kv_ready = j;
           return true;
         };
-        auto issue_s = [&](int g, int j) {
+        // S_g(j) overwrites S_g: the softmax must have pulled the previous
+        // scores of group g into registers (s_free) first.
+        auto issue_s = [&](int g, int j) -> bool {
+          if (s_issued[g] > 0 && !mbar_wait(&s_free[g], (s_issued[g] - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+            fail(kSiteSFree);
+            return false;
+          }
+          ++s_issued[g];
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sQ + (qs * 2 + g) * C::TILE_BYTES);
           const uint32_t k_addr = smem_u32(sK + ((kv_base + j) % kStages) * C::TILE_BYTES);
@@ -298,11 +309,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_f16_ss(tmem_base + g * kBN, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[g]);
+          return true;
         };
         if (!wait_kv(0)) break;
-        for (int g = 0; g < 2; ++g)
+        for (int g = 0; g < 2 && ok; ++g)
           if (it.last[g] > 0) issue_s(g, 0);
         for (int j = 0; j < it.n_kv && ok; ++j) {
+          // S_g(j+1) as soon as group g has pulled S_g(j) into registers, so the
+          // next scores are computed during tile j's exponentials.
+          for (int g = 0; g < 2 && ok; ++g) {
+            if (j + 1 >= it.last[g]) continue;
+            if (!wait_kv(j + 1)) break;
+            if (!issue_s(g, j + 1)) break;
+          }
           for (int g = 0; g < 2 && ok; ++g) {
             if (j >= it.last[g]) continue;
             if (!mbar_wait(&p_full[g], tiles_g[g] & 1, &abort_flag, p.wait_limit_ns)) {
@@ -310,12 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             ++tiles_g[g];
-            // S_g(j+1) first: it overwrites S_g, which the softmax has finished
-            // reading; P_g(j) lives in its own columns, so PV_g(j) can follow.
-            if (j + 1 < it.last[g]) {
-              if (!wait_kv(j + 1)) break;
-              issue_s(g, j + 1);
-            }
             if (j == 0 && o_uses[g] > 0) {
               // the previous item's epilogue of group g must be done reading O_g
               if (!mbar_wait(&o_free[g], (o_uses[g] - 1) & 1, &abort_flag, p.wait_limit_ns)) {
@@ -389,6 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sv[c]);
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);  // the first waits, the rest pin registers
+        // S_g is in registers: the MMA warp may compute the next tile's scores now
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[g]);
         // masking only on the causal diagonal / kv-bound tile; warp-uniform elsewhere
         const bool full = lim >= kBN;
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
