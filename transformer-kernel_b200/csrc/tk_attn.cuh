@@ -259,11 +259,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
       constexpr uint32_t idesc_o = idesc_f16_f32(kBM, HD, false, true);
-      int kv_count = 0;          // KV tiles consumed so far (ring position)
-      int tiles_g[2] = {0, 0};   // tiles processed by each group (s_full / p_full phases)
-      int o_uses[2] = {0, 0};    // items in which each group accumulated O (o_full / o_free phases)
-      int s_issued[2] = {0, 0};  // S_g MMAs issued (s_free phases)
-      int qn = 0;                // items with work consumed so far (Q buffer set = qn & 1)
+      // Per-group counters live in named scalars and every per-group step is
+      // expanded for g = 0 and g = 1 separately, so nothing on this
+      // single-thread critical path is indexed dynamically (local memory).
+      struct Group {
+        int tiles = 0;     // tiles handed over by the softmax (p_full phases)
+        int o_uses = 0;    // items in which O_g was accumulated (o_full / o_free phases)
+        int s_issued = 0;  // S_g MMAs issued (s_free phases)
+      };
+      Group grp0, grp1;
+      int kv_count = 0;  // KV tiles consumed so far (ring position)
+      int qn = 0;        // items with work consumed so far (Q buffer set = qn & 1)
       bool ok = true;
       auto fail = [&](unsigned site) {
         report_error(kDevWaitTimeout, kid * 256 + site);
@@ -272,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
         const Item it = make_item(p, idx, q_tiles, q_pairs);
         if (it.n_kv == 0) continue;
+        const int last0 = it.last[0], last1 = it.last[1];
         const int qs = qn & 1;
         const uint32_t q_phase = (qn >> 1) & 1;
         ++qn;
@@ -293,12 +300,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         // S_g(j) overwrites S_g: the softmax must have pulled the previous
         // scores of group g into registers (s_free) first.
-        auto issue_s = [&](int g, int j) -> bool {
-          if (s_issued[g] > 0 && !mbar_wait(&s_free[g], (s_issued[g] - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+        auto issue_s = [&](Group& gs, const int g, int j) {
+          if (!ok) return;
+          if (!wait_kv(j)) return;
+          if (gs.s_issued > 0 && !mbar_wait(&s_free[g], (gs.s_issued - 1) & 1, &abort_flag, p.wait_limit_ns)) {
             fail(kSiteSFree);
-            return false;
+            return;
           }
-          ++s_issued[g];
+          ++gs.s_issued;
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sQ + (qs * 2 + g) * C::TILE_BYTES);
           const uint32_t k_addr = smem_u32(sK + ((kv_base + j) % kStages) * C::TILE_BYTES);
@@ -309,49 +318,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_f16_ss(tmem_base + g * kBN, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[g]);
-          return true;
         };
-        if (!wait_kv(0)) break;
-        for (int g = 0; g < 2 && ok; ++g)
-          if (it.last[g] > 0) issue_s(g, 0);
+        // O_g += P_g(j) V_j once group g has written P_g(j) (p_full).
+        auto issue_pv = [&](Group& gs, const int g, int j, int last_g, bool last_reader) {
+          if (!ok) return;
+          if (!mbar_wait(&p_full[g], gs.tiles & 1, &abort_flag, p.wait_limit_ns)) {
+            fail(kSiteP);
+            return;
+          }
+          ++gs.tiles;
+          if (j == 0 && gs.o_uses > 0 &&
+              !mbar_wait(&o_free[g], (gs.o_uses - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+            // the previous item's epilogue of group g must be done reading O_g
+            fail(kSiteOFree);
+            return;
+          }
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sV + ((kv_base + j) % kStages) * C::TILE_BYTES);
+#pragma unroll
+          for (int ks = 0; ks < kBN / 16; ++ks) {
+            const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
+            mma_f16_ts(tmem_base + kColO + g * 64, tmem_base + kColP + g * 64 + ks * 8, dv, idesc_o,
+                       (j > 0 || ks > 0) ? 1u : 0u);
+          }
+          mma_commit(&pv_done[g]);  // P_g and O_g free for the softmax of tile j+1
+          if (last_reader) mma_commit(&kv_empty[(kv_base + j) % kStages]);  // K_j / V_j released
+          if (j + 1 == last_g) {
+            mma_commit(&o_full[g]);
+            ++gs.o_uses;
+          }
+        };
+        if (last0 > 0) issue_s(grp0, 0, 0);
+        if (last1 > 0) issue_s(grp1, 1, 0);
         for (int j = 0; j < it.n_kv && ok; ++j) {
           // S_g(j+1) as soon as group g has pulled S_g(j) into registers, so the
           // next scores are computed during tile j's exponentials.
-          for (int g = 0; g < 2 && ok; ++g) {
-            if (j + 1 >= it.last[g]) continue;
-            if (!wait_kv(j + 1)) break;
-            if (!issue_s(g, j + 1)) break;
-          }
-          for (int g = 0; g < 2 && ok; ++g) {
-            if (j >= it.last[g]) continue;
-            if (!mbar_wait(&p_full[g], tiles_g[g] & 1, &abort_flag, p.wait_limit_ns)) {
-              fail(kSiteP);
-              break;
-            }
-            ++tiles_g[g];
-            if (j == 0 && o_uses[g] > 0) {
-              // the previous item's epilogue of group g must be done reading O_g
-              if (!mbar_wait(&o_free[g], (o_uses[g] - 1) & 1, &abort_flag, p.wait_limit_ns)) {
-                fail(kSiteOFree);
-                break;
-              }
-            }
-            tc_fence_after();
-            const uint32_t v_addr = smem_u32(sV + ((kv_base + j) % kStages) * C::TILE_BYTES);
-#pragma unroll
-            for (int ks = 0; ks < kBN / 16; ++ks) {
-              const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
-              mma_f16_ts(tmem_base + kColO + g * 64, tmem_base + kColP + g * 64 + ks * 8, dv, idesc_o,
-                         (j > 0 || ks > 0) ? 1u : 0u);
-            }
-            mma_commit(&pv_done[g]);  // P_g and O_g free for the softmax of tile j+1
-            // the last reader of K_j / V_j releases the stage
-            if (g == 1 || j >= it.last[1]) mma_commit(&kv_empty[(kv_base + j) % kStages]);
-            if (j + 1 == it.last[g]) {
-              mma_commit(&o_full[g]);
-              ++o_uses[g];
-            }
-          }
+          if (j + 1 < last0) issue_s(grp0, 0, j + 1);
+          if (j + 1 < last1) issue_s(grp1, 1, j + 1);
+          // the last reader of K_j / V_j (group 1 when it attends tile j) releases the stage
+          if (j < last0) issue_pv(grp0, 0, j, last0, j >= last1);
+          if (j < last1) issue_pv(grp1, 1, j, last1, true);
         }
         if (!ok) break;
         mma_commit(&q_empty[qs]);  // every S of this item read its Q set
