@@ -79,7 +79,7 @@ class ShardedTransformer(torch.nn.Module):
         self._bufs = {}
         self._mask_owner = self.replicas[0]  # its dense-mask memo (one sync per mask object)
 
-    def _buffers(self, x: torch.Tensor, bounds):
+    def _shard_buffers(self, x: torch.Tensor, bounds):
         key = (tuple(x.shape), x.dtype)
         bufs = self._bufs.get(key)
         if bufs is None:
@@ -99,7 +99,7 @@ class ShardedTransformer(torch.nn.Module):
         B = x.shape[0]
         bounds = [shard_bounds(B, n, r) for r in range(n)]
         out = torch.empty(x.shape, dtype=torch.float32, device=home)
-        bufs = self._buffers(x, bounds)
+        bufs = self._shard_buffers(x, bounds)
         dense = self._mask_owner._prefix_lengths(valid_token_mask) is None
         main = torch.cuda.current_stream(home)
         ready = torch.cuda.Event()
