@@ -154,3 +154,60 @@ def test_gemm_pair_resid_in_place(cuda_device, M, N, K):
     buf = r.cuda()
     tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid", resid=buf, sum_out=buf)
     torch.testing.assert_close(buf.cpu(), r + ref_linear(a, w, b), atol=1e-4, rtol=1e-4)
+
+
+def test_gemm_pair_k_tail(cuda_device):
+    # K = 320: the last 128-wide k stage of the pair kernel is half zero-filled
+    M, N, K = 8192, 2048, 320
+    a, w, b = operands(M, N, K, seed=43)
+    out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "bias")
+    torch.testing.assert_close(out.float().cpu(), ref_linear(a, w, b), atol=2e-3, rtol=2e-2)
+
+
+def test_gemm_pair_strided_out_guard_bands(cuda_device):
+    # fp16 output rows with a stride wider than N inside a guarded buffer: the
+    # TMA stores write exactly the M x N window (M tail clipped).
+    M, N, K, ldo, pad = 9000, 2048, 256, 2048 + 64, 8192
+    a, w, b = operands(M, N, K, seed=47)
+    buf = torch.full((M * ldo + 2 * pad,), 77.0, dtype=torch.float16, device="cuda")
+    out = buf[pad:pad + M * ldo].view(M, ldo)[:, :N]
+    tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "gelu", out=out)
+    torch.cuda.synchronize()
+    host = buf.cpu()
+    assert torch.all(host[:pad] == 77.0) and torch.all(host[-pad:] == 77.0)
+    assert torch.all(host[pad:pad + M * ldo].view(M, ldo)[:, N:] == 77.0)
+    want = F.gelu(ref_linear(a, w, b), approximate="none")
+    torch.testing.assert_close(out.float().cpu(), want, atol=2e-4, rtol=1e-3)
+
+
+def test_gemm_pair_row_len(cuda_device):
+    S, B, N, K = 256, 40, 2048, 256
+    a, w, b = operands(B * S, N, K, seed=53)
+    lengths = (torch.arange(B, dtype=torch.int32) * 37) % (S + 1)
+    out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "gelu", row_len=lengths.cuda(), seq_len=S)
+    pad = (torch.arange(B * S) % S) >= lengths.repeat_interleave(S)
+    got = out.float().cpu()
+    assert torch.all(got[pad] == 0)
+    want = F.gelu(ref_linear(a, w, b), approximate="none")
+    torch.testing.assert_close(got[~pad], want[~pad], atol=2e-4, rtol=1e-3)
+
+
+@pytest.mark.parametrize("row_len", [False, True])
+def test_gemm_pair_resid_out_of_place(cuda_device, row_len):
+    # sum_out != resid (or padded rows): the staged residual epilogue of the pair kernel
+    S, B, N, K = 256, 64, 1024, 512
+    M = B * S
+    a, w, b = operands(M, N, K, seed=59)
+    r = seeded(M, N, seed=60)
+    rc = r.cuda()
+    lengths = (torch.arange(B, dtype=torch.int32) * 53) % (S + 1)
+    kw = dict(row_len=lengths.cuda(), seq_len=S) if row_len else {}
+    s = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid", resid=rc, **kw)
+    want = r + ref_linear(a, w, b)
+    got = s.cpu()
+    if row_len:
+        pad = (torch.arange(M) % S) >= lengths.repeat_interleave(S)
+        assert torch.all(got[pad] == 0)
+        got, want = got[~pad], want[~pad]
+    torch.testing.assert_close(got, want, atol=1e-4, rtol=1e-4)
+    assert torch.equal(rc.cpu(), r)  # resid untouched

@@ -55,18 +55,23 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// fp16 tensor map over a row-major matrix: dims innermost first.
-int make_map_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
-                 const cuuint32_t* box, CUtensorMapSwizzle swz) {
+// Tensor map over a row-major fp16 (or fp32) tensor: dims innermost first.
+int make_map(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank, const cuuint64_t* dims,
+             const cuuint64_t* strides_bytes, const cuuint32_t* box, CUtensorMapSwizzle swz) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(TK_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable from the driver");
   cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   if (rank < 1 || rank > 5) return fail(TK_ERR_INVALID, "tensor map rank %d", rank);
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
+  CUresult r = fn(map, dtype, rank, const_cast<void*>(base), dims, strides_bytes, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TK_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
   return TK_OK;
+}
+
+int make_map_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                 const cuuint32_t* box, CUtensorMapSwizzle swz) {
+  return make_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, base, rank, dims, strides_bytes, box, swz);
 }
 
 struct DeviceInfo {
@@ -136,8 +141,8 @@ int launch_gemm_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mw, const
 }
 
 template <int EPI>
-int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mw, const tk::gemm::Params& p, DeviceInfo* info,
-                     cudaStream_t stream) {
+int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mw, const CUtensorMap& mo, const tk::gemm::Params& p,
+                     DeviceInfo* info, cudaStream_t stream) {
   using C = tk::gemm::PairCfg;
   auto kern = tk::gemm::gemm_pair_kernel<EPI>;
   {
@@ -150,7 +155,7 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mw, const tk::gem
   }
   const int tiles = ((p.M + 255) / 256) * (p.N / 256);
   const int pairs = tiles < info->sms / 2 ? tiles : info->sms / 2;
-  kern<<<2 * pairs, tk::gemm::kThreads, C::SMEM_BYTES, stream>>>(ma, mw, p);
+  kern<<<2 * pairs, tk::gemm::kThreads, C::SMEM_BYTES, stream>>>(ma, mw, mo, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
   return TK_OK;
@@ -320,13 +325,31 @@ int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
   p.out = out; p.ldo = ldo; p.out_f32 = (ln_epi && out_dtype == TK_F32) ? 1 : 0;
   p.gamma = gamma; p.beta = beta; p.eps = eps;
   p.row_len = row_len; p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : 1);
+  p.reduce_add = 0;
   p.wait_limit_ns = g_wait_limit_ns.load();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (pair) {
+    // fp16 outputs leave through TMA stores of 32 x 32 tiles (64-byte swizzle)
+    CUtensorMap mo = ma;  // unused by the staged residual epilogue
+    p.reduce_add = (epilogue == TK_EPI_BIAS_RESID && resid == sum_out && ld_resid == ld_sum && row_len == nullptr);
+    if (p.reduce_add) {
+      // in-place residual update: TMA reduce-add of 32 x 16 fp32 tiles into sum_out
+      cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+      cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_sum) * 4};
+      cuuint32_t box[2] = {16, 32};
+      if (int st = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sum_out, 2, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_64B))
+        return st;
+    } else if (epilogue != TK_EPI_BIAS_RESID) {
+      cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+      cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldo) * 2};
+      cuuint32_t box[2] = {32, 32};
+      if (int st = make_map_f16(&mo, out, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) return st;
+    }
     switch (epilogue) {
-      case TK_EPI_BIAS: return launch_gemm_pair<tk::gemm::kBias>(ma, mw, p, info, s);
-      case TK_EPI_BIAS_GELU: return launch_gemm_pair<tk::gemm::kBiasGelu>(ma, mw, p, info, s);
-      case TK_EPI_BIAS_RESID: return launch_gemm_pair<tk::gemm::kBiasResid>(ma, mw, p, info, s);
+      case TK_EPI_BIAS: return launch_gemm_pair<tk::gemm::kBias>(ma, mw, mo, p, info, s);
+      case TK_EPI_BIAS_GELU: return launch_gemm_pair<tk::gemm::kBiasGelu>(ma, mw, mo, p, info, s);
+      case TK_EPI_BIAS_RESID: return launch_gemm_pair<tk::gemm::kBiasResid>(ma, mw, mo, p, info, s);
     }
   }
   switch (bn) {

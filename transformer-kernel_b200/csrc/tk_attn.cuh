@@ -89,32 +89,6 @@ struct Cfg {
   static constexpr int SMEM_BYTES = TILE_BYTES * (4 + 2 * kStages) + 1024;  // 2 Q sets of 2 tiles
 };
 
-// ---- packed fp32 helpers (sm_100 f32x2 FMA/ADD, 3-input max) ----
-__device__ __forceinline__ void fma2(float& r0, float& r1, float a0, float a1, float b, float c) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "mov.b64 rb, {%4, %4};\n\t"
-      "mov.b64 rc, {%5, %5};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
-      "mov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(r0), "=f"(r1)
-      : "f"(a0), "f"(a1), "f"(b), "f"(c));
-}
-__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
-  asm("{\n\t.reg .b64 ra, rs;\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "mov.b64 rs, {%0, %1};\n\t"
-      "add.rn.f32x2 rs, rs, ra;\n\t"
-      "mov.b64 {%0, %1}, rs;\n\t}"
-      : "+f"(s0), "+f"(s1)
-      : "f"(a0), "f"(a1));
-}
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
 enum : unsigned { kSiteQ = 1, kSiteKV = 2, kSiteS = 3, kSiteP = 4, kSiteO = 5, kSiteEmpty = 6, kSiteOFree = 7,
                   kSiteQEmpty = 8, kSitePv = 9, kSiteSFree = 10 };
 

@@ -52,6 +52,7 @@ struct Params {
   float eps;
   const int* row_len;      // optional per-sequence valid length: rows with
   int seq_len;             //   (row % seq_len) >= row_len[row / seq_len] are zeroed
+  int reduce_add;          // pair kBiasResid: sum_out == resid, no row_len -> TMA reduce-add
   uint64_t wait_limit_ns;
 };
 
@@ -76,30 +77,40 @@ struct Cfg {
 // Exact-form GELU, x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)), as the harness's
 // F.gelu(approximate="none") (src/torch_transformer_benchmark.py:141).
 // erf is evaluated with Abramowitz & Stegun, Handbook of Mathematical
-// Functions, formula 7.1.26: for z >= 0,
-//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^{-z^2},  t = 1/(1 + p z),
-// |error| <= 1.5e-7, extended to z < 0 by oddness. The reciprocal and the
-// exponential use the SFU (rcp.approx, ex2.approx); the result is stored as
-// fp16 (relative rounding 2^-11), far above the approximation error. The
-// GEMM tests compare it with torch's exact erf GELU.
+// Functions, formula 7.1.28: for z >= 0,
+//   erf(z) = 1 - (1 + a1 z + a2 z^2 + ... + a6 z^6)^-16,   |error| <= 3e-7,
+// extended to z < 0 by oddness. With r = (1 + ... + a6 z^6)^-16 and z = |x|/sqrt2,
+//   GELU(x) = 0.5 x + 0.5 |x| (1 - r) = max(x, 0) - 0.5 |x| r,
+// so one reciprocal (SFU rcp.approx) per value and the rest on the FMA pipe,
+// two values per f32x2 instruction. In fp32 the maximum absolute GELU error
+// is below 1e-6 over all x (scanned against double-precision erf); the
+// result is stored as fp16 (relative rounding 2^-11). The GEMM tests compare
+// it with torch's exact erf GELU. Large |x|: the power overflows to +inf,
+// r = 0 and GELU(x) = max(x, 0).
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
-__device__ __forceinline__ float gelu_erf(float v) {
-  constexpr float kP = 0.3275911f;
-  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f, kA4 = -1.453152027f,
-                  kA5 = 1.061405429f;
-  const float z = fabsf(v) * 0.70710678118654752f;
-  const float t = rcp_approx(fmaf(kP, z, 1.f));
-  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, kA5, kA4), kA3), kA2), kA1);
-  const float e = ex2_approx(-z * z * 1.4426950408889634f);
-  const float erf_abs = fmaf(-poly, e, 1.f);
-  const float half_x = 0.5f * v;
-  // 0.5 v (1 + sign(v) erf(|v|/sqrt2))
-  return fmaf(half_x, copysignf(erf_abs, v), half_x);
+__device__ __forceinline__ float2 gelu_erf2(float2 v) {
+  constexpr float kA1 = 0.0705230784f, kA2 = 0.0422820123f, kA3 = 0.0092705272f, kA4 = 0.0001520143f,
+                  kA5 = 0.0002765672f, kA6 = 0.0000430638f;
+  constexpr float kInvSqrt2 = 0.70710678118654752f;
+  const float2 z = make_float2(fabsf(v.x) * kInvSqrt2, fabsf(v.y) * kInvSqrt2);
+  float2 q = ffma2(z, splat2(kA6), splat2(kA5));
+  q = ffma2(q, z, splat2(kA4));
+  q = ffma2(q, z, splat2(kA3));
+  q = ffma2(q, z, splat2(kA2));
+  q = ffma2(q, z, splat2(kA1));
+  q = ffma2(q, z, splat2(1.f));
+  q = fmul2(q, q);  // ^2
+  q = fmul2(q, q);  // ^4
+  q = fmul2(q, q);  // ^8
+  q = fmul2(q, q);  // ^16
+  const float2 r = make_float2(rcp_approx(q.x), rcp_approx(q.y));
+  const float2 neg_half_abs = fmul2(z, splat2(-kInvSqrt2));  // -0.5 |x|
+  return ffma2(neg_half_abs, r, make_float2(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f)));
 }
 
 // Non-LayerNorm epilogue of one 32-row x HALF_N-column slice of an
@@ -168,10 +179,9 @@ __device__ __forceinline__ void staged_epilogue(const Params& p, float* stage, u
               *reinterpret_cast<float4*>(p.sum_out + static_cast<int64_t>(grow) * p.ld_sum + gcol) = sv;
             } else {
               if constexpr (EPI == kBiasGelu) {
-                v.x = gelu_erf(v.x);
-                v.y = gelu_erf(v.y);
-                v.z = gelu_erf(v.z);
-                v.w = gelu_erf(v.w);
+                const float2 g0 = gelu_erf2(make_float2(v.x, v.y));
+                const float2 g1 = gelu_erf2(make_float2(v.z, v.w));
+                v = make_float4(g0.x, g0.y, g1.x, g1.y);
               }
               if (zero) v = make_float4(0.f, 0.f, 0.f, 0.f);
               uint2 o;
@@ -191,6 +201,115 @@ __device__ __forceinline__ void staged_epilogue(const Params& p, float* stage, u
         }
       }
     }
+}
+
+// fp16-output epilogue (kBias / kBiasGelu) of one warp's 32 rows x HALF_N
+// columns, written with TMA stores. Thread = row: each 32-column TMEM chunk
+// gets its bias (and GELU) in registers, is packed to fp16 into a 32 x 32
+// staging tile in the 64-byte swizzle of `map_out` (16-byte unit u of row r
+// sits at unit u ^ ((r >> 1) & 3), so the row-per-lane writes are free of bank
+// conflicts), and lane 0 stores the tile with one cp.async.bulk.tensor. The
+// warp's two staging tiles alternate (`n_stores` counts this warp's stores);
+// a tile is rewritten only after the store that last read it has finished
+// reading. Rows past M are clipped by the tensor map.
+template <int HALF_N, int EPI>
+__device__ __forceinline__ void tma_store_epilogue(const Params& p, const CUtensorMap* map_out, uint8_t* stage,
+                                                   uint32_t t_row, int row_base, int col_base, uint32_t lane,
+                                                   uint32_t& n_stores) {
+  static_assert(EPI == kBias || EPI == kBiasGelu, "fp16-output epilogues only");
+  constexpr int kChunks = HALF_N / 32;
+  const int row = row_base + static_cast<int>(lane);
+  bool zero = false;
+  if (p.row_len != nullptr && row < p.M) zero = (row % p.seq_len) >= p.row_len[row / p.seq_len];
+  const uint32_t sw = (lane >> 1) & 3;
+  uint32_t r[32];
+  tmem_ld32(t_row, r);
+  tmem_ld_wait(r);
+#pragma unroll 1
+  for (int c = 0; c < kChunks; ++c) {
+    const int col0 = col_base + c * 32;
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+    uint32_t h[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 bb = __ldg(b4 + j);
+      float2 v0 = fadd2(make_float2(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1])),
+                        make_float2(bb.x, bb.y));
+      float2 v1 = fadd2(make_float2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
+                        make_float2(bb.z, bb.w));
+      if constexpr (EPI == kBiasGelu) {
+        v0 = gelu_erf2(v0);
+        v1 = gelu_erf2(v1);
+      }
+      h[2 * j + 0] = zero ? 0u : pack_half2(v0.x, v0.y);
+      h[2 * j + 1] = zero ? 0u : pack_half2(v1.x, v1.y);
+    }
+    if (c + 1 < kChunks) tmem_ld32(t_row + (c + 1) * 32, r);  // next chunk lands during the store
+    uint8_t* buf = stage + (n_stores & 1u) * 2048u;
+    if (lane == 0) bulk_wait_read<1>();  // the store issued two chunks ago has read `buf`
+    __syncwarp();
+    uint4* row_ptr = reinterpret_cast<uint4*>(buf + lane * 64u);
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u)
+      row_ptr[u ^ sw] = make_uint4(h[4 * u + 0], h[4 * u + 1], h[4 * u + 2], h[4 * u + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && row_base < p.M) {
+      tma_store_2d(map_out, buf, col0, row_base);
+      bulk_commit();
+    }
+    ++n_stores;
+    if (c + 1 < kChunks) tmem_ld_wait(r);
+  }
+}
+
+// Residual epilogue when the residual stream is updated in place (sum_out ==
+// resid, no padded rows): sum_out += acc + bias by TMA reduce-add, which the
+// L2 performs, so the SM never loads the residual and never waits on it.
+// Thread = row: a 16-column TMEM chunk plus bias goes into a 32 x 16 fp32
+// staging tile in the 64-byte swizzle of `map_sum` (16-byte unit u of row r at
+// u ^ ((r >> 1) & 3)), reduced into global memory by lane 0. The two staging
+// tiles alternate as in tma_store_epilogue. The fp32 sum is
+// resid + (acc + bias), the same operation order as the staged epilogue.
+template <int HALF_N>
+__device__ __forceinline__ void tma_reduce_epilogue(const Params& p, const CUtensorMap* map_sum, uint8_t* stage,
+                                                    uint32_t t_row, int row_base, int col_base, uint32_t lane,
+                                                    uint32_t& n_stores) {
+  constexpr int kChunks = HALF_N / 16;
+  const uint32_t sw = (lane >> 1) & 3;
+  uint32_t r[16];
+  tmem_ld16(t_row, r);
+  tmem_ld_wait(r);
+#pragma unroll 1
+  for (int c = 0; c < kChunks; ++c) {
+    const int col0 = col_base + c * 16;
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+    float4 o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 bb = __ldg(b4 + j);
+      const float2 lo = fadd2(make_float2(__uint_as_float(r[4 * j + 0]), __uint_as_float(r[4 * j + 1])),
+                              make_float2(bb.x, bb.y));
+      const float2 hi = fadd2(make_float2(__uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])),
+                              make_float2(bb.z, bb.w));
+      o[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
+    }
+    if (c + 1 < kChunks) tmem_ld16(t_row + (c + 1) * 16, r);
+    uint8_t* buf = stage + (n_stores & 1u) * 2048u;
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    float4* row_ptr = reinterpret_cast<float4*>(buf + lane * 64u);
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u) row_ptr[u ^ sw] = o[u];
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && row_base < p.M) {
+      tma_reduce_add_2d(map_sum, buf, col0, row_base);
+      bulk_commit();
+    }
+    ++n_stores;
+    if (c + 1 < kChunks) tmem_ld_wait(r);
+  }
 }
 
 // wait sites (error word "where" low byte)
@@ -498,25 +617,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 // CTA-pair variant: a 2-CTA cluster computes 256 x 256 output tiles with
 // tcgen05.mma.cta_group::2 (M = 256 across the pair's TMEM, N = 256). Each
 // CTA stages its own 128 rows of A and its own half (128 rows) of W, so a
-// k-block costs each SM 32 KB of shared memory instead of 48 KB for the same
-// MMA work, and the stage ring is 6 deep. The even CTA issues every MMA;
+// 64-wide k slice costs each SM 32 KB of shared memory instead of 48 KB for
+// the same MMA work. A stage holds a 128-wide k block (two 128-byte swizzle
+// atoms per operand, 64 KB per CTA), three stages deep: fewer, larger stages
+// halve the barrier round trips per MMA and measured 7-9% faster than 64-wide
+// stages six deep. The even CTA issues every MMA;
 // both CTAs' TMA loads complete on the even CTA's stage barrier, and each
-// MMA commit is delivered to both CTAs. Epilogues are per CTA (its 128 rows),
-// identical to the single-CTA kernel. Non-LayerNorm epilogues, N % 256 == 0.
+// MMA commit is delivered to both CTAs. Epilogues are per CTA (its 128 rows):
+// fp16 outputs leave through TMA stores (tma_store_epilogue); an in-place
+// residual update through TMA reduce-add (tma_reduce_epilogue); other
+// residual epilogues through the staged transpose of the single-CTA kernel.
+// The next tile's residual rows are prefetched into L2 a main loop ahead.
+// Non-LayerNorm epilogues, N % 256 == 0.
 // ----------------------------------------------------------------------------
 struct PairCfg {
-  static constexpr int A_BYTES = 128 * kBK * 2;
-  static constexpr int B_BYTES = 128 * kBK * 2;
+  static constexpr int BK = 128;                    // k columns per stage
+  static constexpr int ATOM_BYTES = 128 * kBK * 2;  // 128 rows x one 64-column swizzle atom
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = 128 * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int TMEM_COLS = 512;
   static constexpr int EPI_OFFSET = STAGES * STAGE_BYTES;
-  static constexpr int SMEM_BYTES = EPI_OFFSET + kEpiWarps * kStageBytesPerWarp + 1024;
+  static constexpr int EPI_BYTES_PER_WARP = 4096;  // two 2 KB fp16 store tiles, or one 2 KB fp32 staging tile
+  static constexpr int SMEM_BYTES = EPI_OFFSET + kEpiWarps * EPI_BYTES_PER_WARP + 1024;
+  static_assert(SMEM_BYTES <= 227 * 1024 - 256, "pair kernel shared memory");
 };
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w, Params p) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                     const __grid_constant__ CUtensorMap map_out, Params p) {
   static_assert(EPI != kBiasResidLn, "pair kernel has no LayerNorm epilogue");
   using C = PairCfg;
   constexpr int TN = 256;  // pair tile: 256 rows x 256 columns
@@ -537,7 +668,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int m_tiles = (p.M + 2 * kBM - 1) / (2 * kBM);
   const int n_tiles = p.N / TN;
   const int num_tiles = m_tiles * n_tiles;
-  const int k_blocks = (p.K + kBK - 1) / kBK;
+  const int k_blocks = (p.K + C::BK - 1) / C::BK;
   const unsigned kid = 0x40u + EPI;
 
   if (threadIdx.x == 0) {
@@ -584,8 +715,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + C::A_BYTES;
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * C::STAGE_BYTES);
           const uint32_t full_even = mapa_shared(&full_bar[stage], 0);
-          tma_load_2d_pair(sa, &map_a, full_even, kb * kBK, m0);
-          tma_load_2d_pair(sb, &map_w, full_even, kb * kBK, n0);
+          // columns past K (a K that is not a multiple of 128) are zero-filled
+          const int k0 = kb * C::BK;
+          tma_load_2d_pair(sa, &map_a, full_even, k0, m0);
+          tma_load_2d_pair(sa + C::ATOM_BYTES, &map_a, full_even, k0 + kBK, m0);
+          tma_load_2d_pair(sb, &map_w, full_even, k0, n0);
+          tma_load_2d_pair(sb + C::ATOM_BYTES, &map_w, full_even, k0 + kBK, n0);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -625,9 +760,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t a_addr = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t b_addr = a_addr + C::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
-            const uint64_t db = smem_desc(b_addr + kk * 32, 16, 1024, kLayoutSW128);
+          for (int kk = 0; kk < C::BK / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * C::ATOM_BYTES + (kk & 3) * 32;  // atom, then 16-column step
+            const uint64_t da = smem_desc(a_addr + off, 16, 1024, kLayoutSW128);
+            const uint64_t db = smem_desc(b_addr + off, 16, 1024, kLayoutSW128);
             mma_f16_ss_pair(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           mma_commit_pair(mapa_shared(&empty_bar[stage], 0));
@@ -652,11 +788,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     constexpr int HALF_N = TN / 2;
-    float* stage = reinterpret_cast<float*>(smem + C::EPI_OFFSET) + (warp - 2) * (32 * kStageCols);
+    uint8_t* stage = smem + C::EPI_OFFSET + (warp - 2) * C::EPI_BYTES_PER_WARP;
+    uint32_t n_stores = 0;
     int it = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      if constexpr (EPI == kBiasResid) {
+        // The residual rows of this warp's slice of the next tile go to L2
+        // now, a whole main loop ahead of their use.
+        const int next = tile + npairs;
+        if (next < num_tiles) {
+          const int nrow = (next / n_tiles) * 2 * kBM + static_cast<int>(rank) * kBM + quad * 32 + static_cast<int>(lane);
+          const int ncol = (next % n_tiles) * TN + half * HALF_N;
+          if (nrow < p.M) prefetch_l2_bulk(p.resid + static_cast<int64_t>(nrow) * p.ld_resid + ncol, HALF_N * 4);
+        }
+      }
       if (!mbar_wait_cluster(&acc_full[acc], acc_phase, &abort_flag, p.wait_limit_ns)) {
         report_error(kDevWaitTimeout, kid * 256 + kSiteAccFull);
         abort_flag = 1;
@@ -666,11 +813,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int m0 = (tile / n_tiles) * 2 * kBM + static_cast<int>(rank) * kBM;
       const int n0 = (tile % n_tiles) * TN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * TN + half * HALF_N;
-      staged_epilogue<HALF_N, EPI>(p, stage, t_row, m0 + quad * 32, n0 + half * HALF_N, lane);
+      if constexpr (EPI == kBiasResid) {
+        if (p.reduce_add)
+          tma_reduce_epilogue<HALF_N>(p, &map_out, stage, t_row, m0 + quad * 32, n0 + half * HALF_N, lane, n_stores);
+        else
+          staged_epilogue<HALF_N, EPI>(p, reinterpret_cast<float*>(stage), t_row, m0 + quad * 32,
+                                       n0 + half * HALF_N, lane);
+      } else
+        tma_store_epilogue<HALF_N, EPI>(p, &map_out, stage, t_row, m0 + quad * 32, n0 + half * HALF_N, lane,
+                                        n_stores);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
     }
+    if (lane == 0) bulk_wait_all();  // stores complete before the CTA's shared memory goes away
   }
 
   tc_fence_before();
