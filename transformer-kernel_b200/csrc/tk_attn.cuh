@@ -58,6 +58,27 @@ constexpr int kTmemCols = 512;
 constexpr int kColP = 256;  // P_g at kColP + 64 g (packed fp16 pairs)
 constexpr int kColO = 384;  // O_g at kColO + 64 g (fp32, HD <= 64 columns)
 constexpr float kLazyRescaleLog2 = 8.f;
+// Of every 8 consecutive score columns, this many take 2^x on the FMA pipe
+// (exp2_fma) instead of the SFU: the SFU (16 results/clk/SM) is the
+// softmax's bottleneck at head_dim 64, and the FMA pipe has room.
+constexpr int kExpFmaPer8 = 2;
+
+// 2^x on the FMA/ALU pipes, for x <= 8 (scores minus the running max).
+// Cody-Waite style range reduction x = n + f with n = rint(x), |f| <= 1/2
+// (adding 1.5 * 2^23 rounds x to an integer in the low mantissa bits), then
+// 2^f by a degree-3 polynomial fitted here for minimum maximum relative
+// error on [-1/2, 1/2] (7.5e-5, below the 2^-11 fp16 rounding that P gets),
+// and 2^n added into the exponent field. x is clamped at -126 so the
+// exponent cannot wrap; 2^-126 becomes 0 in the fp16 P.
+__device__ __forceinline__ float exp2_fma(float x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992811f, kC1 = 0.69326099f, kC2 = 0.24261054f, kC3 = 0.05517132f;
+  x = fmaxf(x, -126.f);
+  const float t = x + kRound;
+  const float f = x - (t - kRound);
+  const float q = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
+  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
 
 struct Params {
   __half* out;          // [B, S, ld_out] fp16, head h at columns [h*HD, h*HD+HD)
@@ -426,7 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; ++t) sv[c][t] = __float_as_uint(ex2_approx(__uint_as_float(sv[c][t])));
+          for (int t = 0; t < 32; ++t) {
+            const float x = __uint_as_float(sv[c][t]);
+            sv[c][t] = __float_as_uint((t & 7) >= 8 - kExpFmaPer8 ? exp2_fma(x) : ex2_approx(x));
+          }
         if (!full) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
