@@ -21,7 +21,14 @@ pinned host memory and the fp32 output copied back every step.
 ``--impl reference`` times the fp32 CPU forward of the reference model (the
 oracle's restatement of BaselineTransformer; the reference is pure Python
 and does not travel to the GPU box) on the host cores, one bounded
-batch-slice per step.
+batch-slice per step. For C5 (S = 100,000) the CPU forward of even one
+sequence is ~10^14 FLOP, so the CPU figure is extrapolated from the exact
+query-chunked oracle: two runs over all keys with R and 2R query rows give
+the per-row cost and the all-row (LayerNorm / K / V) cost, scaled to S rows.
+
+C1 and C2 fit in L2: their steps are timed one by one with an L2 flush
+(a 512 MB write) between them, outside the events. Larger configurations
+exceed L2 and are timed back to back.
 """
 
 from __future__ import annotations
@@ -49,7 +56,12 @@ CONFIGS = {
     "C2": (1, 512, 512, 8, 2048, 4, True),
     "C3": (256, 256, 1024, 16, 4096, 4, False),
     "C4": (8, 8192, 1024, 16, 4096, 2, True),
+    "C5": (32, 100000, 1024, 16, 4096, 1, True),
 }
+# timed steps when --steps is not given (C5: ~1 s per forward on one GPU)
+DEFAULT_STEPS = {"C5": 3}
+# configurations whose working set fits in the 126 MB L2: flush it between steps
+L2_RESIDENT = ("C1", "C2")
 METRIC = "layer-stack forward tokens/s"
 
 
@@ -177,16 +189,52 @@ def cpu_forward_rate(cfg_tuple, seconds, sample_batch, steps=None):
     return nb * S / med, threads, f"{nb} of {B} sequences x {n} forwards, median {med * 1e3:.1f} ms", times
 
 
+def cpu_long_seq_rate(cfg_tuple, rows=1024, reps=2):
+    """fp32 CPU tokens/s for one long sequence, extrapolated: the exact
+    query-chunked oracle is run over all S keys with 8 and with `rows`
+    evenly spread query rows (best of `reps` each); t(R) = t0 + R * t_row
+    gives the per-row cost t_row and the all-row part t0 (LayerNorm, K and V
+    projections), and one sequence costs t0 + S * t_row. Returns
+    (tokens_per_s, threads, description, [seconds per sequence])."""
+    from oracle import StackConfig, generate_random_case, init_params, stack_forward_rows
+
+    B, S, d, H, ffn, L, causal = cfg_tuple
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = StackConfig(1, S, d, H, ffn, L, causal)
+    params = init_params(cfg, seed=0)
+    x, _ = generate_random_case(cfg, seed=1234 + 100000)
+
+    def timed(n):
+        idx = torch.linspace(0, S - 1, n).round().long()
+        t0 = time.perf_counter()
+        stack_forward_rows(params, cfg, x, idx, None, q_chunk=64)
+        return time.perf_counter() - t0
+
+    timed(8)  # warm
+    t_lo = min(timed(8) for _ in range(reps))
+    t_hi = min(timed(rows) for _ in range(reps))
+    t_row = max(t_hi - t_lo, 1e-9) / (rows - 8)
+    t_seq = max(t_lo - 8 * t_row, 0.0) + S * t_row
+    desc = (f"1 of {B} sequences, extrapolated: query-chunked oracle over all {S} keys with 8 and {rows} "
+            f"spread query rows (best of {reps}: {t_lo:.2f} s, {t_hi:.2f} s) -> {t_seq:.1f} s per sequence")
+    return S / t_seq, threads, desc, [t_seq]
+
+
 def run_reference(args, cfg_tuple, rank):
     """--impl reference: the CPU fp32 reference forward on the host cores."""
     if rank != 0:
         return
     B, S, d, H, ffn, L, causal = cfg_tuple
-    sample = 8 if args.config in ("C3",) else (1 if args.config == "C4" else B)
-    rate, threads, desc, times = cpu_forward_rate(cfg_tuple, 0, sample, steps=args.warmup + args.steps)
-    times = times[args.warmup:] or times
-    med = statistics.median(times)
-    value = min(B, sample) * S / med
+    if args.config == "C5":
+        value, threads, desc, times = cpu_long_seq_rate(cfg_tuple)
+        med, sample = times[0], 1
+    else:
+        sample = 8 if args.config in ("C3",) else (1 if args.config == "C4" else B)
+        rate, threads, desc, times = cpu_forward_rate(cfg_tuple, 0, sample, steps=args.warmup + args.steps)
+        times = times[args.warmup:] or times
+        med = statistics.median(times)
+        value = min(B, sample) * S / med
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": med * 1e3 * (B / min(B, sample)), "higher_is_better": True,
@@ -195,17 +243,31 @@ def run_reference(args, cfg_tuple, rank):
         "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
                    "global_batch": B, "seq_len": S, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": f"{min(B, sample)} of {B} sequences per step"},
+                         "sample": desc if args.config == "C5" else f"{min(B, sample)} of {B} sequences per step"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+def measured_traffic(config, kernel, batch):
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
+    summary profiles/dram_traffic.json, captured on a smaller batch of the
+    same configuration and scaled by rows (the kernels' traffic is
+    proportional to the batch); None when no capture covers it."""
+    path = ROOT / "profiles" / "dram_traffic.json"
+    try:
+        table = json.loads(path.read_text())
+        entry = table[config][kernel]
+    except (OSError, KeyError, ValueError):
+        return None
+    return entry["bytes_per_launch"] * batch / entry["batch"]
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=60)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 60; C5: 3)")
+    ap.add_argument("--warmup", type=int, default=None, help="untimed warm-up steps (default 5; C5: 3)")
     ap.add_argument("--config", default="C3", choices=sorted(CONFIGS))
     ap.add_argument("--batch", type=int, default=0, help="override the config's batch (small profiling cases)")
     ap.add_argument("--impl", default="tk", choices=["tk", "reference"])
@@ -213,6 +275,10 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=4, help="batch slices of the streamed end-to-end forward")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = DEFAULT_STEPS.get(args.config, 60)
+    if args.warmup is None:
+        args.warmup = 3 if args.config == "C5" else 5
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
@@ -244,7 +310,10 @@ def main() -> int:
     torch.manual_seed(0)
     # The public graph-replaying drop-in (the reference's --cuda-graphs
     # path); its eager superclass forward is used for the per-kernel trace.
-    model = cuda_graphs.GraphedTransformer(ocfg).to(dev).eval()
+    # C5 (one ~1 s forward per step) runs the eager drop-in: a graph saves
+    # nothing there and its static input/output copies would cost 26 GB.
+    graphed = args.config != "C5"
+    model = (cuda_graphs.GraphedTransformer(ocfg) if graphed else optimized.OptimizedTransformer(ocfg)).to(dev).eval()
     eager_forward = optimized.OptimizedTransformer.forward
     gen = torch.Generator().manual_seed(1234 + 100000)
     x_host = torch.randn(B, S, d, generator=gen).pin_memory()
@@ -265,26 +334,44 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    flush = args.config in L2_RESIDENT
+    scratch = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if flush else None
+
     with torch.inference_mode():
         # ---- graph capture (untimed), then device-resident timing ----
-        for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 1):
-            model(x, mask)
+        if graphed:
+            for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 1):
+                model(x, mask)
         for _ in range(args.warmup):
             model(x, mask)
         tk.check_device_errors(dev)
         barrier()
         torch.cuda.synchronize(dev)
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with Clocks(local) as clk:
             clk.mark("t_start")
-            t0.record(stream)
-            for _ in range(args.steps):
-                model(x, mask)
-            t1.record(stream)
-            torch.cuda.synchronize(dev)
+            if flush:
+                # one event pair per step; the L2 flush between steps is outside them
+                pairs = []
+                for _ in range(args.steps):
+                    scratch.fill_(1)
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record(stream)
+                    model(x, mask)
+                    b.record(stream)
+                    pairs.append((a, b))
+                torch.cuda.synchronize(dev)
+                local_ms = sum(a.elapsed_time(b) for a, b in pairs) / args.steps
+            else:
+                t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                t0.record(stream)
+                for _ in range(args.steps):
+                    model(x, mask)
+                t1.record(stream)
+                torch.cuda.synchronize(dev)
+                local_ms = t0.elapsed_time(t1) / args.steps
             clk.mark("t_end")
         barrier()
-        ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+        ms = max_over_ranks(local_ms)
         clocks = clk.summary()
         tk.check_device_errors(dev)
 
@@ -348,7 +435,7 @@ def main() -> int:
         achieved = T * d * (4 + 2) / (avg_ms * 1e-3) / 1e9
         roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "peak_kind": f"{peak_kind} copy"}
-    roof["traffic"] = None
+    roof["traffic"] = measured_traffic(args.config, dom, B)
     share = {k: round(v / sum(totals.values()), 4) for k, v in sorted(totals.items(), key=lambda kv: -kv[1])}
     kernels_ms = {k: round(statistics.fmean(v), 5) for k, v in per.items()}
 
@@ -359,8 +446,11 @@ def main() -> int:
 
     cpu = None
     if not args.no_cpu_baseline:
-        sample = 8 if args.config == "C3" else (1 if args.config == "C4" else B)
-        rate, threads, desc, _ = cpu_forward_rate(cfg_tuple, args.cpu_seconds, sample)
+        if args.config == "C5":
+            rate, threads, desc, _ = cpu_long_seq_rate(cfg_tuple)
+        else:
+            sample = 8 if args.config == "C3" else (1 if args.config == "C4" else B)
+            rate, threads, desc, _ = cpu_forward_rate(cfg_tuple, args.cpu_seconds, sample)
         cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
 
     line = {
@@ -369,7 +459,8 @@ def main() -> int:
         "vs_baseline": None, "dtype": "f16 operands / f32 accumulate+residual", "data": "synthetic",
         "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
                    "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world} (batch-sharded, no collective)",
-                   "l2": "inputs and activations > 126 MB L2; no flush"},
+                   "l2": ("L2 flushed between steps (512 MB write outside the events)" if flush
+                          else "inputs and activations > 126 MB L2; no flush")},
         "e2e": {"value": world * tokens * 1000.0 / e2e_ms, "unit": "tokens/s", "ms_per_step": e2e_ms,
                 "path": f"forward_from_host, {chunks} streamed slices" if streamed else "copy in, graph replay, copy out",
                 "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 4},

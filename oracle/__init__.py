@@ -25,4 +25,5 @@ from .baseline import (  # noqa: F401
     init_params,
     layer_norm_reference,
     stack_forward,
+    stack_forward_rows,
 )

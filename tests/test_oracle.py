@@ -12,7 +12,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from oracle import StackConfig, compare_outputs, generate_random_case, init_params, stack_forward
+from oracle import StackConfig, compare_outputs, generate_random_case, init_params, stack_forward, stack_forward_rows
 
 SMALL = ["tiny_causal", "tiny_bidir", "tiny_padded", "ragged_s"]
 LARGE = ["c1_reference_case1", "c2_small_batch", "c3_slice_b2_l1", "c4_slice_s1024_l1"]
@@ -69,3 +69,19 @@ def test_acceptance_rule_catches_a_planted_error(golden):
     bad[1, 3, 7] += 0.01 + 0.05 * bad[1, 3, 7].abs()
     r = compare_outputs(entry["out"], bad)
     assert not r.passed and r.failed_elements == 1 and r.worst_index == (1, 3, 7)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_query_chunked_rows_match_stack_forward(causal):
+    """The query-chunked row-subset oracle (the long-sequence proxy) equals
+    the full-matrix oracle, masks included, for every row subset and chunk."""
+    cfg = StackConfig(2, 300, 64, 4, 128, 2, causal)
+    params = init_params(cfg, seed=0)
+    x, mask = generate_random_case(cfg, seed=5)
+    mask[1, 200:] = False
+    full = stack_forward(params, cfg, x, mask)
+    rows = torch.tensor([0, 1, 63, 64, 150, 199, 200, 299])
+    got = stack_forward_rows(params, cfg, x, rows, mask, q_chunk=3)
+    torch.testing.assert_close(got, full[:, rows], atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(stack_forward_rows(params, cfg, x, None, mask, q_chunk=64), full,
+                               atol=1e-6, rtol=1e-6)
