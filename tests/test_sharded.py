@@ -77,9 +77,16 @@ def test_sharded_forward_matches_single_gpu(cuda_device, mode):
     shard = sharded.ShardedTransformer(model, devices)
     x, mask = generate_random_case(cfg, 21)
     xd, md = x.cuda(), mask.cuda()
+    x2, _ = generate_random_case(cfg, 22)
+    x2d = x2.cuda()
     with torch.inference_mode():
         want = model(xd, md)
+        want2 = model(x2d, md)
         for _ in range(12):  # past graph capture in every replica
             got = shard(xd, md)
+        got2 = shard(x2d, md).clone()  # replays the captured graphs on new input
+        got_again = shard(xd, md)
         torch.cuda.synchronize()
     torch.testing.assert_close(got, want, atol=0, rtol=0)
+    torch.testing.assert_close(got2, want2, atol=0, rtol=0)
+    torch.testing.assert_close(got_again, want, atol=0, rtol=0)

@@ -27,13 +27,14 @@ WARMUP_BEFORE_CAPTURE = 8
 
 
 class _GraphState:
-    __slots__ = ("eager_calls", "graph", "static_x", "static_out")
+    __slots__ = ("eager_calls", "graph", "static_x", "static_out", "buffers")
 
     def __init__(self) -> None:
         self.eager_calls = 0
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.static_x: Optional[torch.Tensor] = None
         self.static_out: Optional[torch.Tensor] = None
+        self.buffers = None  # activation buffers the graph's kernels use
 
 
 class GraphedTransformer(OptimizedTransformer):
@@ -72,7 +73,16 @@ class GraphedTransformer(OptimizedTransformer):
             for _ in range(2):
                 super().forward(state.static_x, mask)
         torch.cuda.current_stream(x.device).wait_stream(side)
+        # The activation buffers are allocated before capture: nothing is
+        # allocated while the stream captures (with peer access enabled between
+        # GPUs, a device allocation is not permitted during capture).
+        state.buffers = self._pin_activations(state.static_x)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            state.static_out = super().forward(state.static_x, mask)
+        try:
+            # capture on a stream of x's device (torch's default capture
+            # stream belongs to whichever device first captured)
+            with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=x.device)):
+                state.static_out = super().forward(state.static_x, mask)
+        finally:
+            self._pin_activations(None)
         state.graph = graph

@@ -228,6 +228,37 @@ class OptimizedTransformer(nn.Module):
             tk.check_device_errors(x.device)
         return out if out.dtype == x.dtype else out.to(x.dtype)
 
+    def _activations(self, B: int, S: int, d: int, ffn: int, dev: torch.device):
+        """Activation buffers of one forward: residual stream fp32 [T, d], h
+        fp16 [T, d], qkv fp16 [T, 3d], ctx fp16 [B, S, d], u fp16 [T, ffn] and
+        the output fp32 [T, d]. Fresh from the caching allocator, unless a set
+        for exactly this shape was pinned with `_pin_activations` (graph
+        capture allocates nothing while the stream is capturing)."""
+        key = (B, S, d, ffn, dev)
+        pinned = getattr(self, "_pinned_activations", None)
+        if pinned is not None and pinned[0] == key:
+            return pinned[1]
+        T = B * S
+        return (torch.empty((T, d), dtype=torch.float32, device=dev),
+                torch.empty((T, d), dtype=torch.float16, device=dev),
+                torch.empty((T, 3 * d), dtype=torch.float16, device=dev),
+                torch.empty((B, S, d), dtype=torch.float16, device=dev),
+                torch.empty((T, ffn), dtype=torch.float16, device=dev),
+                torch.empty((T, d), dtype=torch.float32, device=dev))
+
+    def _pin_activations(self, x: torch.Tensor):
+        """Allocate and pin the activation buffers for inputs shaped like x
+        (``None`` unpins). Returns the pinned buffers."""
+        if x is None:
+            self._pinned_activations = None
+            return None
+        B, S, d = x.shape
+        ffn = self.layers[0].ffn_in.weight.shape[0]
+        self._pinned_activations = None
+        bufs = self._activations(B, S, d, ffn, x.device)
+        self._pinned_activations = ((B, S, d, ffn, x.device), bufs)
+        return bufs
+
     def _run(self, x: torch.Tensor, lengths: Optional[torch.Tensor], out: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, S, d = x.shape
         T = B * S
@@ -241,15 +272,8 @@ class OptimizedTransformer(nn.Module):
             xin = xin.to(torch.float32).contiguous()
         seq = S if lengths is not None else 0
 
-        res = torch.empty((T, d), dtype=torch.float32, device=dev)
-        h = torch.empty((T, d), dtype=torch.float16, device=dev)
-        qkv = torch.empty((T, 3 * d), dtype=torch.float16, device=dev)
-        ctx = torch.empty((B, S, d), dtype=torch.float16, device=dev)
-        u = torch.empty((T, ffn), dtype=torch.float16, device=dev)
-        if out is None:
-            out = torch.empty((T, d), dtype=torch.float32, device=dev)
-        else:
-            out = out.view(T, d)
+        res, h, qkv, ctx, u, out_ws = self._activations(B, S, d, ffn, dev)
+        out = out_ws if out is None else out.view(T, d)
         stream = tk.stream_handle(dev)
 
         def layer_norm(src, w, b, eps, dst, zero_padded):
