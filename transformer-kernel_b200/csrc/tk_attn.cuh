@@ -397,32 +397,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.causal) lim = min(lim, q_idx - k0 + 1);
         lim = max(0, min(kBN, lim));
 
-        // the whole 128-column score row in registers: one TMEM round trip
-        uint32_t sv[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sv[c]);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);  // the first waits, the rest pin registers
-        // S_g is in registers: the MMA warp may compute the next tile's scores now
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[g]);
-        // masking only on the causal diagonal / kv-bound tile; warp-uniform elsewhere
-        const bool full = lim >= kBN;
+        // The score row is handled 64 columns at a time, so only half of it
+        // (plus its packed P) is ever live in registers: pass 1 takes the row
+        // max over both halves (the second half stays in registers), pass 2
+        // exponentiates the second half, then reloads and exponentiates the
+        // first; S_g is released to the MMA warp after that reload.
+        const bool full = lim >= kBN;  // masking only on the causal diagonal / kv-bound tile
+        uint32_t sv[2][32];
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (full) {
+        auto row_max = [&](const int col0) {
+          if (full) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+            for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int t = 0; t < 32; t += 2)
-              mx4[(t >> 1) & 3] = max3(mx4[(t >> 1) & 3], __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]));
-        } else {
+              for (int t = 0; t < 32; t += 2)
+                mx4[(t >> 1) & 3] = max3(mx4[(t >> 1) & 3], __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]));
+          } else {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+            for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int t = 0; t < 32; ++t)
-              if (c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
-        }
+              for (int t = 0; t < 32; ++t)
+                if (col0 + c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
+          }
+        };
+        tmem_ld32(t_s, sv[0]);
+        tmem_ld32(t_s + 32, sv[1]);
+        tmem_ld_wait(sv[0]);
+        tmem_ld_wait(sv[1]);
+        row_max(0);
+        tmem_ld32(t_s + 64, sv[0]);
+        tmem_ld32(t_s + 96, sv[1]);
+        tmem_ld_wait(sv[0]);
+        tmem_ld_wait(sv[1]);
+        row_max(64);
         const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         float m_use = m;
         float alpha = 1.f;
@@ -433,45 +440,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
-        // P = 2^(s*c - m*c) in independent passes (all exponents, then all
-        // ex2 back to back on the SFU, then sums and fp16 packing), in place.
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            float x0, x1;
-            fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
-            sv[c][t] = __float_as_uint(x0);
-            sv[c][t + 1] = __float_as_uint(x1);
-          }
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const float x = __uint_as_float(sv[c][t]);
-            sv[c][t] = __float_as_uint((t & 7) >= 8 - kExpFmaPer8 ? exp2_fma(x) : ex2_approx(x));
-          }
-        if (!full) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int t = 0; t < 32; ++t)
-              if (c * 32 + t >= lim) sv[c][t] = 0u;
-        }
         float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[4][16];
+        // P = 2^(s*c - m*c) for the 64 columns in sv starting at col0, in
+        // independent passes (exponents, then ex2, then sums and fp16
+        // packing), stored to P_g's TMEM columns.
+        auto exp_half = [&](const int col0) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; t += 2) {
-            const float p0 = __uint_as_float(sv[c][t]), p1 = __uint_as_float(sv[c][t + 1]);
-            const int a = ((t >> 1) & 3) * 2;
-            add2(rs[a], rs[a + 1], p0, p1);
-            pk[c][t / 2] = pack_half2(p0, p1);
+            for (int t = 0; t < 32; t += 2) {
+              float x0, x1;
+              fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
+              sv[c][t] = __float_as_uint(x0);
+              sv[c][t + 1] = __float_as_uint(x1);
+            }
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              const float x = __uint_as_float(sv[c][t]);
+              sv[c][t] = __float_as_uint((t & 7) >= 8 - kExpFmaPer8 ? exp2_fma(x) : ex2_approx(x));
+            }
+          if (!full) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int t = 0; t < 32; ++t)
+                if (col0 + c * 32 + t >= lim) sv[c][t] = 0u;
           }
-        const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
-        // PV_g of the previous tile (issued after S_g(j)) reads P_g and writes
-        // O_g: it must be complete before P_g is overwritten or O_g rescaled.
+          uint32_t pk[2][16];
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int t = 0; t < 32; t += 2) {
+              const float p0 = __uint_as_float(sv[c][t]), p1 = __uint_as_float(sv[c][t + 1]);
+              const int a = ((t >> 1) & 3) * 2;
+              add2(rs[a], rs[a + 1], p0, p1);
+              pk[c][t / 2] = pack_half2(p0, p1);
+            }
+#pragma unroll
+          for (int c = 0; c < 2; ++c) tmem_st16(t_p + col0 / 2 + c * 16, pk[c]);
+        };
+        // PV_g of the previous tile reads P_g and writes O_g: it must be
+        // complete before P_g is overwritten or O_g rescaled.
         if (tiles > 0) {
           if (!mbar_wait(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
             report_error(kDevWaitTimeout, kid * 256 + kSitePv);
@@ -481,8 +492,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_st16(t_p + c * 16, pk[c]);
+        exp_half(64);
+        tmem_ld32(t_s, sv[0]);
+        tmem_ld32(t_s + 32, sv[1]);
+        tmem_ld_wait(sv[0]);
+        tmem_ld_wait(sv[1]);
+        // S_g is fully in registers: the MMA warp may compute the next tile's scores
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[g]);
+        exp_half(0);
+        const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
         const bool need = (j > 0) && (alpha != 1.f);
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
