@@ -122,6 +122,15 @@ TK_API int tk_check_device_errors(void* stream);
  * (default 2e9). Returns the previous value. */
 TK_API uint64_t tk_set_wait_limit_ns(uint64_t ns);
 
+/* Launch later launch-bound (small) kernels with programmatic stream
+ * serialization (1, the default) or plainly (0); returns the previous
+ * setting. With it, such a kernel may be scheduled while the previous kernel
+ * on the stream drains, and waits on the device (griddepcontrol.wait) for
+ * that kernel's results before touching global memory. Large kernels always
+ * launch plainly. No counterpart in the reference (its kernels are launched
+ * by Triton / PyTorch); results are identical either way. */
+TK_API int tk_set_programmatic_launch(int enable);
+
 /* Test hook for failure detection: launches one CTA that waits on an
  * mbarrier nothing arrives on, with the configured limit, so the wait gives
  * up and records TK_ERR_TIMEOUT in the error word. Never faults. */

@@ -42,6 +42,7 @@ SIGNATURES = {
     "tk_attn_supported": (_I, [_I64]),
     "tk_check_device_errors": (_I, [_P]),
     "tk_set_wait_limit_ns": (_U64, [_U64]),
+    "tk_set_programmatic_launch": (_I, [_I]),
     "tk_selftest_wait_timeout": (_I, [_P]),
     "tk_last_error": (ctypes.c_char_p, []),
     "tk_version": (ctypes.c_char_p, []),
@@ -122,6 +123,13 @@ def check_device_errors(device: Optional[torch.device] = None) -> None:
 
 def set_wait_limit_ns(ns: int) -> int:
     return int(lib().tk_set_wait_limit_ns(int(ns)))
+
+
+def set_programmatic_launch(enable: bool) -> bool:
+    """Launch later launch-bound (small) kernels with programmatic dependent
+    launch (default on; large kernels always launch plainly). Returns the
+    previous setting."""
+    return bool(lib().tk_set_programmatic_launch(1 if enable else 0))
 
 
 def version() -> str:

@@ -21,6 +21,35 @@ namespace {
 
 thread_local std::string g_last_error;
 std::atomic<uint64_t> g_wait_limit_ns{2000000000ull};
+std::atomic<int> g_programmatic_launch{1};
+
+// Launch-bound (small) kernels are launched with programmatic stream
+// serialization (when enabled): such a kernel may be scheduled while the
+// previous kernel in the stream drains, runs its prologue (barrier init,
+// TMEM allocation, tensor-map prefetch), then waits in griddepcontrol.wait
+// for that kernel's results. Inside a CUDA graph the dependency becomes a
+// programmatic edge. Measured on one B200: C2 (batch 1, seq 512) forward
+// -10%; applied to the large C3 kernels it cost ~2% (early-scheduled CTAs
+// share SMs with the previous kernel's tail), so large kernels launch plainly.
+constexpr double kSmallGemmMNK = 8.6e9;        // M * N * K
+constexpr double kSmallAttnWork = 2.2e9;       // B * H * S * S * hd
+constexpr double kSmallLnElements = 4.2e6;     // rows * d
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool small,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (small && g_programmatic_launch.load()) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 int fail(int status, const char* fmt, ...) {
   char buf[512];
@@ -122,8 +151,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mw, const tk::gemm::Pa
   }
   const int tiles = ((p.M + tk::gemm::kBM - 1) / tk::gemm::kBM) * ((p.N + BN - 1) / BN);
   const int grid = tiles < info->sms ? tiles : info->sms;
-  kern<<<grid, tk::gemm::kThreads, C::SMEM_BYTES, stream>>>(ma, mw, p);
-  cudaError_t e = cudaGetLastError();
+  const bool small = static_cast<double>(p.M) * p.N * p.K <= kSmallGemmMNK;
+  cudaError_t e = launch(kern, dim3(grid), dim3(tk::gemm::kThreads), C::SMEM_BYTES, stream, small, ma, mw, p);
   if (e != cudaSuccess) return cuda_fail(e, "gemm launch");
   return TK_OK;
 }
@@ -155,8 +184,8 @@ int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mw, const CUtenso
   }
   const int tiles = ((p.M + 255) / 256) * (p.N / 256);
   const int pairs = tiles < info->sms / 2 ? tiles : info->sms / 2;
-  kern<<<2 * pairs, tk::gemm::kThreads, C::SMEM_BYTES, stream>>>(ma, mw, mo, p);
-  cudaError_t e = cudaGetLastError();
+  const bool small = static_cast<double>(p.M) * p.N * p.K <= kSmallGemmMNK;
+  cudaError_t e = launch(kern, dim3(2 * pairs), dim3(tk::gemm::kThreads), C::SMEM_BYTES, stream, small, ma, mw, mo, p);
   if (e != cudaSuccess) return cuda_fail(e, "gemm pair launch");
   return TK_OK;
 }
@@ -189,6 +218,8 @@ const char* tk_last_error(void) { return g_last_error.c_str(); }
 const char* tk_version(void) { return "tk_b200 0.1 (sm_100a)"; }
 
 uint64_t tk_set_wait_limit_ns(uint64_t ns) { return g_wait_limit_ns.exchange(ns); }
+
+int tk_set_programmatic_launch(int enable) { return g_programmatic_launch.exchange(enable ? 1 : 0); }
 
 int tk_layernorm_supported(int64_t d) { return d >= 1 && d <= 8192 ? 1 : 0; }
 
@@ -230,18 +261,20 @@ int tk_layernorm(const void* x, int x_dtype, int64_t ld_x, const void* y, int y_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool xf = x_dtype == TK_F32, yf = (y == nullptr) || y_dtype == TK_F32, of = out_dtype == TK_F32;
 
-#define TK_LN_DISPATCH(KERNEL, GRID, ...)                                                         \
-  do {                                                                                          \
-    if (xf && yf && of) KERNEL<__VA_ARGS__ float, float, float, float><<<GRID, 256, 0, s>>>(a);  \
-    else if (xf && yf && !of) KERNEL<__VA_ARGS__ float, float, float, __half><<<GRID, 256, 0, s>>>(a); \
-    else if (xf && !yf && of) KERNEL<__VA_ARGS__ float, __half, float, float><<<GRID, 256, 0, s>>>(a); \
-    else if (xf && !yf && !of) KERNEL<__VA_ARGS__ float, __half, float, __half><<<GRID, 256, 0, s>>>(a); \
-    else if (!xf && yf && of) KERNEL<__VA_ARGS__ __half, float, __half, float><<<GRID, 256, 0, s>>>(a); \
-    else if (!xf && yf && !of) KERNEL<__VA_ARGS__ __half, float, __half, __half><<<GRID, 256, 0, s>>>(a); \
-    else if (!xf && !yf && of) KERNEL<__VA_ARGS__ __half, __half, __half, float><<<GRID, 256, 0, s>>>(a); \
-    else KERNEL<__VA_ARGS__ __half, __half, __half, __half><<<GRID, 256, 0, s>>>(a);              \
+#define TK_LN_DISPATCH(KERNEL, GRID, ...)                                                    \
+  do {                                                                                     \
+    if (xf && yf && of) e = launch(KERNEL<__VA_ARGS__ float, float, float, float>, dim3(GRID), dim3(256), 0, s, small, a); \
+    else if (xf && yf && !of) e = launch(KERNEL<__VA_ARGS__ float, float, float, __half>, dim3(GRID), dim3(256), 0, s, small, a); \
+    else if (xf && !yf && of) e = launch(KERNEL<__VA_ARGS__ float, __half, float, float>, dim3(GRID), dim3(256), 0, s, small, a); \
+    else if (xf && !yf && !of) e = launch(KERNEL<__VA_ARGS__ float, __half, float, __half>, dim3(GRID), dim3(256), 0, s, small, a); \
+    else if (!xf && yf && of) e = launch(KERNEL<__VA_ARGS__ __half, float, __half, float>, dim3(GRID), dim3(256), 0, s, small, a); \
+    else if (!xf && yf && !of) e = launch(KERNEL<__VA_ARGS__ __half, float, __half, __half>, dim3(GRID), dim3(256), 0, s, small, a); \
+    else if (!xf && !yf && of) e = launch(KERNEL<__VA_ARGS__ __half, __half, __half, float>, dim3(GRID), dim3(256), 0, s, small, a); \
+    else e = launch(KERNEL<__VA_ARGS__ __half, __half, __half, __half>, dim3(GRID), dim3(256), 0, s, small, a); \
   } while (0)
 
+  cudaError_t e = cudaSuccess;
+  const bool small = static_cast<double>(rows) * d <= kSmallLnElements;
   if (d <= 1024) {
     const int64_t warps_needed = rows;
     int64_t blocks = (warps_needed + 7) / 8;
@@ -257,7 +290,6 @@ int tk_layernorm(const void* x, int x_dtype, int64_t ld_x, const void* y, int y_
     TK_LN_DISPATCH(tk::ln::ln_cta_rows, grid, );
   }
 #undef TK_LN_DISPATCH
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tk_layernorm launch");
   return TK_OK;
 }
@@ -414,6 +446,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
   // persistent: one CTA per SM over the (b, h, query-tile pair) work items
   const int64_t items = B * H * ((q_tiles + 1) / 2);
   const unsigned grid = static_cast<unsigned>(items < info->sms ? items : info->sms);
+  const bool small = static_cast<double>(B) * H * S * S * hd <= kSmallAttnWork;
   cudaError_t e;
   if (hd == 64) {
     auto kern = tk::attn::attn_fwd_kernel<64>;
@@ -425,7 +458,8 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
         info->attn_attr_set[1] = true;
       }
     }
-    kern<<<grid, tk::attn::kThreads, tk::attn::Cfg<64>::SMEM_BYTES, s>>>(maps[0], maps[1], maps[2], p);
+    e = launch(kern, dim3(grid), dim3(tk::attn::kThreads), tk::attn::Cfg<64>::SMEM_BYTES, s, small, maps[0], maps[1],
+               maps[2], p);
   } else {
     auto kern = tk::attn::attn_fwd_kernel<32>;
     {
@@ -436,9 +470,10 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
         info->attn_attr_set[0] = true;
       }
     }
-    kern<<<grid, tk::attn::kThreads, tk::attn::Cfg<32>::SMEM_BYTES, s>>>(maps[0], maps[1], maps[2], p);
+    e = launch(kern, dim3(grid), dim3(tk::attn::kThreads), tk::attn::Cfg<32>::SMEM_BYTES, s, small, maps[0], maps[1],
+               maps[2], p);
   }
-  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tk_attn_fwd launch");
   return TK_OK;
 }

@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  grid_dep_wait();  // the previous kernel's outputs are complete and visible
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -242,6 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           load_tile(sV + s * C::TILE_BYTES, &map_v, &kv_full[s], p, j * kBN, it.h, it.b);
         }
       }
+      // all of this CTA's loads are issued: the next kernel may be scheduled
+      grid_dep_launch();
       if (!ok) {
         // let copies already in flight land before the CTA can exit
         for (int t = max(0, kv_count - kStages); t < kv_count; ++t)

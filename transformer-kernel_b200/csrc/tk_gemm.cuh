@@ -367,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  grid_dep_wait();  // the previous kernel's outputs are complete and visible
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -395,6 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // all of this CTA's loads are issued: the next kernel may be scheduled
+      grid_dep_launch();
       if (!ok) {
         // Let the copies already in flight land before the CTA can exit:
         // drain every stage that the MMA side has not consumed (bounded).
@@ -692,6 +695,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // barrier inits and TMEM allocation visible to the peer
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  grid_dep_wait();  // the previous kernel's outputs are complete and visible
 
   if (warp == 0) {
     // ---------------- TMA producer (both CTAs) ----------------
@@ -727,6 +731,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // all of this CTA's loads are issued: the next kernel may be scheduled
+      grid_dep_launch();
       (void)ok;
     }
     __syncwarp();

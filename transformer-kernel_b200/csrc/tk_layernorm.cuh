@@ -17,6 +17,8 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "tk_ptx.cuh"
+
 namespace tk {
 namespace ln {
 
@@ -93,6 +95,7 @@ __device__ __forceinline__ bool row_is_padding(const Args& a, int64_t row) {
 // NV = groups of 4 columns per lane; d <= NV * 128.
 template <int NV, typename TX, typename TY, typename TS, typename TH>
 __global__ void __launch_bounds__(256, 3) ln_warp_rows(Args a) {
+  grid_dep_wait();  // the previous kernel's outputs are complete and visible
   const int lane = threadIdx.x & 31;
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -155,6 +158,7 @@ __global__ void __launch_bounds__(256, 3) ln_warp_rows(Args a) {
 // One 256-thread CTA per row, d <= 8192 (8 groups of 4 per thread).
 template <typename TX, typename TY, typename TS, typename TH>
 __global__ void __launch_bounds__(256) ln_cta_rows(Args a) {
+  grid_dep_wait();
   constexpr int NV = 8;
   __shared__ float red[8];
   const int d = static_cast<int>(a.d);

@@ -171,6 +171,15 @@ __device__ __forceinline__ void bulk_wait_read() {
 // Wait until all of this thread's bulk groups are complete.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream is still
+// running; grid_dep_wait() blocks until that kernel has completed and its
+// memory is visible (a no-op when there is no such dependency), so every
+// kernel calls it before its first access to global data. grid_dep_launch()
+// lets the next kernel's CTAs be scheduled (its prologue overlaps our tail).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Hint: bring `bytes` (multiple of 16; 16-byte aligned address) of global
 // memory into L2. No completion to wait for.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* gptr, uint32_t bytes) {
