@@ -37,7 +37,8 @@ def test_version_and_probes():
     lib = tk.lib()
     assert b"sm_100a" in lib.tk_version()
     assert lib.tk_attn_supported(32) == 1 and lib.tk_attn_supported(64) == 1
-    assert lib.tk_attn_supported(128) == 0 and lib.tk_attn_supported(8) == 0
+    assert lib.tk_attn_supported(8) == 1 and lib.tk_attn_supported(16) == 1
+    assert lib.tk_attn_supported(128) == 0 and lib.tk_attn_supported(24) == 0
     assert lib.tk_layernorm_supported(1) == 1 and lib.tk_layernorm_supported(8192) == 1
     assert lib.tk_layernorm_supported(8193) == 0 and lib.tk_layernorm_supported(0) == 0
 

@@ -48,6 +48,11 @@ CONFIGS = {
     "small_d64_bidir": StackConfig(2, 16, 64, 2, 128, 2, False),
     "ragged_s100_d128": StackConfig(2, 100, 128, 4, 256, 1, True),
     "d256_hd64": StackConfig(2, 300, 256, 4, 512, 2, True),
+    # appendix shapes of the reference's sweep with small heads
+    # (configs/shapes.json cases 7 and 11: head_dim 8; d 128 / 8 heads: 16)
+    "appendix7_d32_hd8": StackConfig(8, 128, 32, 4, 32, 4, True),
+    "appendix11_d128_h16_hd8": StackConfig(8, 128, 128, 16, 128, 4, True),
+    "d128_h8_hd16": StackConfig(4, 200, 128, 8, 256, 2, True),
 }
 
 

@@ -106,7 +106,7 @@ int make_map_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t*
 struct DeviceInfo {
   int sms = 0;
   bool gemm_attr_set[4][4] = {};
-  bool attn_attr_set[2] = {};
+  bool attn_attr_set[3] = {};
 };
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
@@ -223,7 +223,9 @@ int tk_set_programmatic_launch(int enable) { return g_programmatic_launch.exchan
 
 int tk_layernorm_supported(int64_t d) { return d >= 1 && d <= 8192 ? 1 : 0; }
 
-int tk_attn_supported(int64_t head_dim) { return head_dim == 32 || head_dim == 64 ? 1 : 0; }
+int tk_attn_supported(int64_t head_dim) {
+  return head_dim == 8 || head_dim == 16 || head_dim == 32 || head_dim == 64 ? 1 : 0;
+}
 
 int tk_layernorm(const void* x, int x_dtype, int64_t ld_x, const void* y, int y_dtype, int64_t ld_y, void* sum_out,
                  int64_t ld_sum, const float* gamma, const float* beta, float eps, void* out, int out_dtype,
@@ -400,7 +402,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
     return fail(TK_ERR_INVALID, "tk_attn_fwd: null pointer");
   if (B <= 0 || S <= 0 || H <= 0 || hd <= 0) return fail(TK_ERR_INVALID, "tk_attn_fwd: non-positive size");
   if (!tk_attn_supported(hd))
-    return fail(TK_ERR_UNSUPPORTED, "tk_attn_fwd: head_dim %lld not in {32,64}", (long long)hd);
+    return fail(TK_ERR_UNSUPPORTED, "tk_attn_fwd: head_dim %lld not in {8,16,32,64}", (long long)hd);
   if (stride_b <= 0 || stride_h <= 0 || stride_s <= 0 || stride_b % 8 || stride_h % 8 || stride_s % 8 ||
       !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
     return fail(TK_ERR_INVALID, "tk_attn_fwd: q/k/v need 16-byte aligned bases and strides (multiples of 8 elements)");
@@ -426,11 +428,15 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
                         static_cast<cuuint64_t>(mid_dim[1]), static_cast<cuuint64_t>(B)};
   cuuint64_t strides[3] = {static_cast<cuuint64_t>(mid_stride[0]) * 2, static_cast<cuuint64_t>(mid_stride[1]) * 2,
                            static_cast<cuuint64_t>(stride_b) * 2};
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(hd), heads_inner ? 1u : 128u, heads_inner ? 128u : 1u, 1};
+  // head_dim 8 runs the 16-wide kernel: the box is 16 columns wide and TMA
+  // fills the 8 columns past the tensor's inner dimension with zeros.
+  const int64_t hd_k = hd < 16 ? 16 : hd;
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(hd_k), heads_inner ? 1u : 128u, heads_inner ? 128u : 1u, 1};
+  const CUtensorMapSwizzle swz = hd_k == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : hd_k == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_32B;
   for (int i = 0; i < 3; ++i)
-    if (int st = make_map_f16(&maps[i], bases[i], 4, dims, strides, box,
-                              hd == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B))
-      return st;
+    if (int st = make_map_f16(&maps[i], bases[i], 4, dims, strides, box, swz)) return st;
   tk::attn::Params p;
   p.out = static_cast<__half*>(out);
   p.ld_out = ld_out;
@@ -441,38 +447,31 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
   p.causal = causal ? 1 : 0;
   p.kv_len = kv_len;
   p.heads_inner = heads_inner ? 1 : 0;
+  p.hd = static_cast<int>(hd);
   p.wait_limit_ns = g_wait_limit_ns.load();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // persistent: one CTA per SM over the (b, h, query-tile pair) work items
   const int64_t items = B * H * ((q_tiles + 1) / 2);
   const unsigned grid = static_cast<unsigned>(items < info->sms ? items : info->sms);
   const bool small = static_cast<double>(B) * H * S * S * hd <= kSmallAttnWork;
+  auto run = [&](auto kern, int slot, int smem_bytes) -> cudaError_t {
+    {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      if (!info->attn_attr_set[slot]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        if (e != cudaSuccess) return e;
+        info->attn_attr_set[slot] = true;
+      }
+    }
+    return launch(kern, dim3(grid), dim3(tk::attn::kThreads), smem_bytes, s, small, maps[0], maps[1], maps[2], p);
+  };
   cudaError_t e;
-  if (hd == 64) {
-    auto kern = tk::attn::attn_fwd_kernel<64>;
-    {
-      std::lock_guard<std::mutex> lk(g_dev_mu);
-      if (!info->attn_attr_set[1]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tk::attn::Cfg<64>::SMEM_BYTES);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn)");
-        info->attn_attr_set[1] = true;
-      }
-    }
-    e = launch(kern, dim3(grid), dim3(tk::attn::kThreads), tk::attn::Cfg<64>::SMEM_BYTES, s, small, maps[0], maps[1],
-               maps[2], p);
-  } else {
-    auto kern = tk::attn::attn_fwd_kernel<32>;
-    {
-      std::lock_guard<std::mutex> lk(g_dev_mu);
-      if (!info->attn_attr_set[0]) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tk::attn::Cfg<32>::SMEM_BYTES);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn)");
-        info->attn_attr_set[0] = true;
-      }
-    }
-    e = launch(kern, dim3(grid), dim3(tk::attn::kThreads), tk::attn::Cfg<32>::SMEM_BYTES, s, small, maps[0], maps[1],
-               maps[2], p);
-  }
+  if (hd_k == 64)
+    e = run(tk::attn::attn_fwd_kernel<64>, 2, tk::attn::Cfg<64>::SMEM_BYTES);
+  else if (hd_k == 32)
+    e = run(tk::attn::attn_fwd_kernel<32>, 1, tk::attn::Cfg<32>::SMEM_BYTES);
+  else
+    e = run(tk::attn::attn_fwd_kernel<16>, 0, tk::attn::Cfg<16>::SMEM_BYTES);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tk_attn_fwd launch");
   return TK_OK;

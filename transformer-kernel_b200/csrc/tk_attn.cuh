@@ -88,6 +88,7 @@ struct Params {
   int causal;
   const int* kv_len;    // optional [B]: keys >= kv_len[b] are masked
   int heads_inner;      // tensor-map dim order {hd, H, S, B} (1) or {hd, S, H, B} (0)
+  int hd;               // head_dim of the data: HD, or 8 for the HD = 16 kernel (zero-padded by TMA)
   uint64_t wait_limit_ns;
 };
 
@@ -102,9 +103,9 @@ __device__ __forceinline__ void load_tile(void* dst, const CUtensorMap* map, uin
 
 template <int HD>
 struct Cfg {
-  static_assert(HD == 32 || HD == 64, "head_dim");
+  static_assert(HD == 16 || HD == 32 || HD == 64, "head_dim");
   static constexpr int ROW_BYTES = HD * 2;                     // swizzle span
-  static constexpr SmemLayout LAYOUT = HD == 64 ? kLayoutSW128 : kLayoutSW64;
+  static constexpr SmemLayout LAYOUT = HD == 64 ? kLayoutSW128 : HD == 32 ? kLayoutSW64 : kLayoutSW32;
   static constexpr int TILE_BYTES = kBM * ROW_BYTES;           // Q, K or V tile
   static constexpr int SBO = 8 * ROW_BYTES;                    // 8-row core-matrix group
   static constexpr int SMEM_BYTES = TILE_BYTES * (4 + 2 * kStages) + 1024;  // 2 Q sets of 2 tiles
@@ -538,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (tq < q_tiles) {
         const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
-        __half* dst = p.out + (static_cast<int64_t>(it.b) * p.S + q_idx) * p.ld_out + it.h * HD;
+        __half* dst = p.out + (static_cast<int64_t>(it.b) * p.S + q_idx) * p.ld_out + it.h * p.hd;
 #pragma unroll
         for (int c = 0; c < HD; c += 16) {
           uint32_t o[16];
@@ -560,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             w1.z = pack_half2(__uint_as_float(o[12]) * inv_l, __uint_as_float(o[13]) * inv_l);
             w1.w = pack_half2(__uint_as_float(o[14]) * inv_l, __uint_as_float(o[15]) * inv_l);
             reinterpret_cast<uint4*>(dst + c)[0] = w0;
-            reinterpret_cast<uint4*>(dst + c)[1] = w1;
+            if (c + 16 <= p.hd) reinterpret_cast<uint4*>(dst + c)[1] = w1;  // head_dim 8: columns 8..15 are padding
           }
         }
       }
