@@ -100,7 +100,8 @@ TK_API int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw,
  *   scale  : multiplies q.k after the product (the harness uses hd**-0.5)
  *   causal : mask keys j > query i
  *   kv_len : optional int32 [B]; keys >= kv_len[b] are masked
- * hd in {8, 16, 32, 64} (8 runs the 16-wide kernel; TMA zero-fills the padding). */
+ * hd in {8, 16, 32, 64, 128, 256} (8 runs the 16-wide kernel with TMA zero-filling
+ * the padding; 128 and 256 run a chunked one-tile-per-CTA kernel). */
 TK_API int tk_attn_fwd(const void* q, const void* k, const void* v,
                 int64_t stride_b, int64_t stride_h, int64_t stride_s,
                 void* out, int64_t ld_out,

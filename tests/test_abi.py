@@ -38,7 +38,8 @@ def test_version_and_probes():
     assert b"sm_100a" in lib.tk_version()
     assert lib.tk_attn_supported(32) == 1 and lib.tk_attn_supported(64) == 1
     assert lib.tk_attn_supported(8) == 1 and lib.tk_attn_supported(16) == 1
-    assert lib.tk_attn_supported(128) == 0 and lib.tk_attn_supported(24) == 0
+    assert lib.tk_attn_supported(128) == 1 and lib.tk_attn_supported(256) == 1
+    assert lib.tk_attn_supported(96) == 0 and lib.tk_attn_supported(24) == 0
     assert lib.tk_layernorm_supported(1) == 1 and lib.tk_layernorm_supported(8192) == 1
     assert lib.tk_layernorm_supported(8193) == 0 and lib.tk_layernorm_supported(0) == 0
 
@@ -73,7 +74,7 @@ def test_gemm_rejects_bad_arguments_on_host(args, status):
 
 def test_attention_rejects_unsupported_head_dim_on_host():
     lib = tk.lib()
-    rc = lib.tk_attn_fwd(16, 16, 16, 3 * 128 * 512, 128, 3 * 512, 16, 512, 1, 128, 4, 128, 0.1, 1, None, None)
+    rc = lib.tk_attn_fwd(16, 16, 16, 3 * 96 * 384, 96, 3 * 384, 16, 384, 1, 128, 4, 96, 0.1, 1, None, None)
     assert rc == -2 and b"head_dim" in lib.tk_last_error()
 
 

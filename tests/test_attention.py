@@ -2,8 +2,8 @@
 (src/test_triton_kernels.py:125-216): fp32 scores scaled after q.k, -inf
 mask, fp32 softmax, PV. Tolerance atol 2e-3 / rtol 2e-2 as in the
 reference's attention tests. Shapes follow the reference's list restricted
-to the head dims this kernel takes (8, 16, 32, 64; 8 runs zero-padded to 16);
-others must be refused."""
+to the head dims these kernels take (8, 16, 32, 64, 128, 256; 8 runs
+zero-padded to 16, 128 and 256 the chunked kernel); others must be refused."""
 
 from __future__ import annotations
 
@@ -23,7 +23,8 @@ def seeded(*shape, seed=0, dtype=torch.float16):
 
 
 SHAPES = [(2, 4, 128, 32), (2, 4, 96, 32), (1, 2, 128, 64), (1, 4, 32, 64), (2, 3, 384, 64), (1, 2, 1000, 64),
-          (3, 2, 257, 32), (2, 4, 128, 16), (1, 3, 300, 16), (2, 4, 128, 8), (1, 16, 200, 8)]
+          (3, 2, 257, 32), (2, 4, 128, 16), (1, 3, 300, 16), (2, 4, 128, 8), (1, 16, 200, 8),
+          (2, 1, 128, 128), (1, 2, 520, 128), (2, 2, 128, 256), (1, 1, 300, 256)]
 
 
 def run(q, k, v, causal, kv_len=None):
@@ -100,8 +101,10 @@ def test_supported_probes(cuda_device):
     assert kernels.attention_supported(64, torch.float16, dev)
     assert kernels.attention_supported(8, torch.float16, dev)
     assert kernels.attention_supported(16, torch.float16, dev)
-    assert not kernels.attention_supported(128, torch.float16, dev)
+    assert kernels.attention_supported(128, torch.float16, dev)
+    assert kernels.attention_supported(256, torch.float16, dev)
+    assert not kernels.attention_supported(96, torch.float16, dev)
     assert not kernels.attention_supported(64, torch.float32, dev)
-    q = seeded(1, 1, 64, 128).cuda()
+    q = seeded(1, 1, 64, 96).cuda()
     with pytest.raises(tk.TKError):
         kernels.flash_attention(q, q, q, 0.1, True)

@@ -53,6 +53,9 @@ CONFIGS = {
     "appendix7_d32_hd8": StackConfig(8, 128, 32, 4, 32, 4, True),
     "appendix11_d128_h16_hd8": StackConfig(8, 128, 128, 16, 128, 4, True),
     "d128_h8_hd16": StackConfig(4, 200, 128, 8, 256, 2, True),
+    # configs/shapes.json case 9 (one head of 128) and case 8 (4 heads of 256), batch cut
+    "appendix9_d128_h1_hd128": StackConfig(16, 128, 128, 1, 128, 4, True),
+    "appendix8_d1024_h4_hd256": StackConfig(4, 128, 1024, 4, 1024, 4, True),
 }
 
 

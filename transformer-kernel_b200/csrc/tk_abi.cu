@@ -12,6 +12,7 @@
 #include <string>
 
 #include "tk_attn.cuh"
+#include "tk_attn_wide.cuh"
 #include "tk_gemm.cuh"
 #include "tk_layernorm.cuh"
 #include "tk_ptx.cuh"
@@ -106,7 +107,7 @@ int make_map_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t*
 struct DeviceInfo {
   int sms = 0;
   bool gemm_attr_set[4][4] = {};
-  bool attn_attr_set[3] = {};
+  bool attn_attr_set[5] = {};
 };
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
@@ -224,7 +225,9 @@ int tk_set_programmatic_launch(int enable) { return g_programmatic_launch.exchan
 int tk_layernorm_supported(int64_t d) { return d >= 1 && d <= 8192 ? 1 : 0; }
 
 int tk_attn_supported(int64_t head_dim) {
-  return head_dim == 8 || head_dim == 16 || head_dim == 32 || head_dim == 64 ? 1 : 0;
+  return head_dim == 8 || head_dim == 16 || head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256
+             ? 1
+             : 0;
 }
 
 int tk_layernorm(const void* x, int x_dtype, int64_t ld_x, const void* y, int y_dtype, int64_t ld_y, void* sum_out,
@@ -402,7 +405,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
     return fail(TK_ERR_INVALID, "tk_attn_fwd: null pointer");
   if (B <= 0 || S <= 0 || H <= 0 || hd <= 0) return fail(TK_ERR_INVALID, "tk_attn_fwd: non-positive size");
   if (!tk_attn_supported(hd))
-    return fail(TK_ERR_UNSUPPORTED, "tk_attn_fwd: head_dim %lld not in {8,16,32,64}", (long long)hd);
+    return fail(TK_ERR_UNSUPPORTED, "tk_attn_fwd: head_dim %lld not in {8,16,32,64,128,256}", (long long)hd);
   if (stride_b <= 0 || stride_h <= 0 || stride_s <= 0 || stride_b % 8 || stride_h % 8 || stride_s % 8 ||
       !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16))
     return fail(TK_ERR_INVALID, "tk_attn_fwd: q/k/v need 16-byte aligned bases and strides (multiples of 8 elements)");
@@ -430,9 +433,12 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
                            static_cast<cuuint64_t>(stride_b) * 2};
   // head_dim 8 runs the 16-wide kernel: the box is 16 columns wide and TMA
   // fills the 8 columns past the tensor's inner dimension with zeros.
+  // head_dim 128 / 256 run the chunked kernel: boxes of 64 columns.
   const int64_t hd_k = hd < 16 ? 16 : hd;
-  cuuint32_t box[4] = {static_cast<cuuint32_t>(hd_k), heads_inner ? 1u : 128u, heads_inner ? 128u : 1u, 1};
-  const CUtensorMapSwizzle swz = hd_k == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+  const bool wide = hd_k > 64;
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(wide ? 64 : hd_k), heads_inner ? 1u : 128u, heads_inner ? 128u : 1u,
+                       1};
+  const CUtensorMapSwizzle swz = (hd_k == 64 || wide) ? CU_TENSOR_MAP_SWIZZLE_128B
                                  : hd_k == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                               : CU_TENSOR_MAP_SWIZZLE_32B;
   for (int i = 0; i < 3; ++i)
@@ -454,7 +460,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
   const int64_t items = B * H * ((q_tiles + 1) / 2);
   const unsigned grid = static_cast<unsigned>(items < info->sms ? items : info->sms);
   const bool small = static_cast<double>(B) * H * S * S * hd <= kSmallAttnWork;
-  auto run = [&](auto kern, int slot, int smem_bytes) -> cudaError_t {
+  auto run = [&](auto kern, int slot, int smem_bytes, unsigned grid_x, unsigned threads) -> cudaError_t {
     {
       std::lock_guard<std::mutex> lk(g_dev_mu);
       if (!info->attn_attr_set[slot]) {
@@ -463,15 +469,22 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
         info->attn_attr_set[slot] = true;
       }
     }
-    return launch(kern, dim3(grid), dim3(tk::attn::kThreads), smem_bytes, s, small, maps[0], maps[1], maps[2], p);
+    return launch(kern, dim3(grid_x), dim3(threads), smem_bytes, s, small, maps[0], maps[1], maps[2], p);
   };
   cudaError_t e;
-  if (hd_k == 64)
-    e = run(tk::attn::attn_fwd_kernel<64>, 2, tk::attn::Cfg<64>::SMEM_BYTES);
+  // chunked kernel: one CTA per (b, h, query tile)
+  const unsigned wide_grid = static_cast<unsigned>(B * H * q_tiles);
+  constexpr unsigned kT = tk::attn::kThreads, kTw = tk::attn::wide::kThreads;
+  if (hd_k == 256)
+    e = run(tk::attn::wide::attn_fwd_wide_kernel<256>, 4, tk::attn::wide::Cfg<256>::SMEM_BYTES, wide_grid, kTw);
+  else if (hd_k == 128)
+    e = run(tk::attn::wide::attn_fwd_wide_kernel<128>, 3, tk::attn::wide::Cfg<128>::SMEM_BYTES, wide_grid, kTw);
+  else if (hd_k == 64)
+    e = run(tk::attn::attn_fwd_kernel<64>, 2, tk::attn::Cfg<64>::SMEM_BYTES, grid, kT);
   else if (hd_k == 32)
-    e = run(tk::attn::attn_fwd_kernel<32>, 1, tk::attn::Cfg<32>::SMEM_BYTES);
+    e = run(tk::attn::attn_fwd_kernel<32>, 1, tk::attn::Cfg<32>::SMEM_BYTES, grid, kT);
   else
-    e = run(tk::attn::attn_fwd_kernel<16>, 0, tk::attn::Cfg<16>::SMEM_BYTES);
+    e = run(tk::attn::attn_fwd_kernel<16>, 0, tk::attn::Cfg<16>::SMEM_BYTES, grid, kT);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tk_attn_fwd launch");
   return TK_OK;
