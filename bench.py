@@ -21,10 +21,13 @@ pinned host memory and the fp32 output copied back every step.
 ``--impl reference`` times the fp32 CPU forward of the reference model (the
 oracle's restatement of BaselineTransformer; the reference is pure Python
 and does not travel to the GPU box) on the host cores, one bounded
-batch-slice per step. For C5 (S = 100,000) the CPU forward of even one
-sequence is ~10^14 FLOP, so the CPU figure is extrapolated from the exact
-query-chunked oracle: two runs over all keys with R and 2R query rows give
-the per-row cost and the all-row (LayerNorm / K / V) cost, scaled to S rows.
+batch-slice per step. For C5 and A14 (S = 100,000) the CPU forward of even
+one sequence is ~10^14 FLOP per layer, so the CPU figure is extrapolated from
+the exact query-chunked oracle: two one-layer runs over all keys with 8 and R
+query rows give the per-row cost and the all-row (LayerNorm / K / V) cost,
+scaled to S rows and L layers. A14 is the reference's case 14
+(configs/shapes.json: batch 32, seq 100000, d 1024, 16 heads, ffn 1024, 2
+layers).
 
 C1 and C2 fit in L2: their steps are timed one by one with an L2 flush
 (a 512 MB write) between them, outside the events. Larger configurations
@@ -57,9 +60,11 @@ CONFIGS = {
     "C3": (256, 256, 1024, 16, 4096, 4, False),
     "C4": (8, 8192, 1024, 16, 4096, 2, True),
     "C5": (32, 100000, 1024, 16, 4096, 1, True),
+    # configs/shapes.json case 14: the reference's out-of-core case (2 layers, ffn 1024)
+    "A14": (32, 100000, 1024, 16, 1024, 2, True),
 }
 # timed steps when --steps is not given (C5: ~1 s per forward on one GPU)
-DEFAULT_STEPS = {"C5": 3}
+DEFAULT_STEPS = {"C5": 3, "A14": 3}
 # configurations whose working set fits in the 126 MB L2: flush it between steps
 L2_RESIDENT = ("C1", "C2")
 METRIC = "layer-stack forward tokens/s"
@@ -191,17 +196,18 @@ def cpu_forward_rate(cfg_tuple, seconds, sample_batch, steps=None):
 
 def cpu_long_seq_rate(cfg_tuple, rows=1024, reps=2):
     """fp32 CPU tokens/s for one long sequence, extrapolated: the exact
-    query-chunked oracle is run over all S keys with 8 and with `rows`
-    evenly spread query rows (best of `reps` each); t(R) = t0 + R * t_row
-    gives the per-row cost t_row and the all-row part t0 (LayerNorm, K and V
-    projections), and one sequence costs t0 + S * t_row. Returns
-    (tokens_per_s, threads, description, [seconds per sequence])."""
+    query-chunked oracle is run for one layer over all S keys with 8 and with
+    `rows` evenly spread query rows (best of `reps` each); t(R) = t0 + R *
+    t_row gives the per-row cost t_row and the all-row part t0 (LayerNorm, K
+    and V projections); one layer of one sequence costs t0 + S * t_row, and
+    the L layers of the stack L times that (every layer does the same work).
+    Returns (tokens_per_s, threads, description, [seconds per sequence])."""
     from oracle import StackConfig, generate_random_case, init_params, stack_forward_rows
 
     B, S, d, H, ffn, L, causal = cfg_tuple
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cfg = StackConfig(1, S, d, H, ffn, L, causal)
+    cfg = StackConfig(1, S, d, H, ffn, 1, causal)
     params = init_params(cfg, seed=0)
     x, _ = generate_random_case(cfg, seed=1234 + 100000)
 
@@ -215,9 +221,10 @@ def cpu_long_seq_rate(cfg_tuple, rows=1024, reps=2):
     t_lo = min(timed(8) for _ in range(reps))
     t_hi = min(timed(rows) for _ in range(reps))
     t_row = max(t_hi - t_lo, 1e-9) / (rows - 8)
-    t_seq = max(t_lo - 8 * t_row, 0.0) + S * t_row
-    desc = (f"1 of {B} sequences, extrapolated: query-chunked oracle over all {S} keys with 8 and {rows} "
-            f"spread query rows (best of {reps}: {t_lo:.2f} s, {t_hi:.2f} s) -> {t_seq:.1f} s per sequence")
+    t_seq = L * (max(t_lo - 8 * t_row, 0.0) + S * t_row)
+    desc = (f"1 of {B} sequences, extrapolated: query-chunked oracle, one layer over all {S} keys with 8 and "
+            f"{rows} spread query rows (best of {reps}: {t_lo:.2f} s, {t_hi:.2f} s), x {L} layers -> "
+            f"{t_seq:.1f} s per sequence")
     return S / t_seq, threads, desc, [t_seq]
 
 
@@ -226,7 +233,7 @@ def run_reference(args, cfg_tuple, rank):
     if rank != 0:
         return
     B, S, d, H, ffn, L, causal = cfg_tuple
-    if args.config == "C5":
+    if args.config in ("C5", "A14"):
         value, threads, desc, times = cpu_long_seq_rate(cfg_tuple)
         med, sample = times[0], 1
     else:
@@ -243,7 +250,7 @@ def run_reference(args, cfg_tuple, rank):
         "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
                    "global_batch": B, "seq_len": S, "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": desc if args.config == "C5" else f"{min(B, sample)} of {B} sequences per step"},
+                         "sample": desc if args.config in ("C5", "A14") else f"{min(B, sample)} of {B} sequences per step"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -278,7 +285,7 @@ def main() -> int:
     if args.steps is None:
         args.steps = DEFAULT_STEPS.get(args.config, 60)
     if args.warmup is None:
-        args.warmup = 3 if args.config == "C5" else 5
+        args.warmup = 3 if args.config in ("C5", "A14") else 5
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
 
@@ -312,7 +319,7 @@ def main() -> int:
     # path); its eager superclass forward is used for the per-kernel trace.
     # C5 (one ~1 s forward per step) runs the eager drop-in: a graph saves
     # nothing there and its static input/output copies would cost 26 GB.
-    graphed = args.config != "C5"
+    graphed = args.config not in ("C5", "A14")
     model = (cuda_graphs.GraphedTransformer(ocfg) if graphed else optimized.OptimizedTransformer(ocfg)).to(dev).eval()
     eager_forward = optimized.OptimizedTransformer.forward
     gen = torch.Generator().manual_seed(1234 + 100000)
@@ -446,7 +453,7 @@ def main() -> int:
 
     cpu = None
     if not args.no_cpu_baseline:
-        if args.config == "C5":
+        if args.config in ("C5", "A14"):
             rate, threads, desc, _ = cpu_long_seq_rate(cfg_tuple)
         else:
             sample = 8 if args.config == "C3" else (1 if args.config == "C4" else B)

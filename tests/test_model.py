@@ -173,3 +173,21 @@ def test_forward_from_host_padded(cuda_device):
         torch.cuda.synchronize()
     r = compare_outputs(stack_forward(params, cfg, x, mask), out)
     assert r.passed, r
+
+
+def test_appendix6_batch_10000_spot_sequences(cuda_device):
+    """configs/shapes.json case 6: batch 10000 (1.28 M token rows). Batch rows
+    are independent, so the full-batch GPU forward is checked on a seeded
+    sample of sequences against the oracle run on those sequences alone."""
+    cfg = StackConfig(10000, 128, 128, 4, 128, 4, True)
+    params, model = build(cfg)
+    x, mask = generate_random_case(cfg, 1234)
+    with torch.inference_mode():
+        out = model(x.cuda(), mask.cuda()).cpu()
+    g = torch.Generator().manual_seed(3)
+    pick = torch.randperm(cfg.batch_size, generator=g)[:24].sort().values
+    pick = torch.cat([pick, torch.tensor([0, cfg.batch_size - 1])])
+    sub = StackConfig(len(pick), 128, 128, 4, 128, 4, True)
+    ref = stack_forward(params, sub, x[pick], mask[pick])
+    r = compare_outputs(ref, out[pick], RTOL, ATOL)
+    assert r.passed, str(r)
