@@ -63,6 +63,11 @@ CONFIGS = {
     # configs/shapes.json case 14: the reference's out-of-core case (2 layers, ffn 1024)
     "A14": (32, 100000, 1024, 16, 1024, 2, True),
 }
+# The reference's published numbers for the same metric and shape (one T4):
+# C1 is appendix case 1 (pass-2 default, 1.405 ms = 5.83 M tokens/s,
+# results/pass2-default.json); A14 is appendix case 14 (155.4 s per forward,
+# 20,597 tokens/s, results/case14-full.json). No other config was published.
+PUBLISHED_TOKENS_PER_S = {"C1": 5.83e6, "A14": 20597.0}
 # timed steps when --steps is not given (C5: ~1 s per forward on one GPU)
 DEFAULT_STEPS = {"C5": 3, "A14": 3}
 # configurations whose working set fits in the 126 MB L2: flush it between steps
@@ -463,7 +468,9 @@ def main() -> int:
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16 operands / f32 accumulate+residual", "data": "synthetic",
+        "vs_baseline": (value / PUBLISHED_TOKENS_PER_S[args.config]
+                        if args.config in PUBLISHED_TOKENS_PER_S and args.batch == 0 else None),
+        "dtype": "f16 operands / f32 accumulate+residual", "data": "synthetic",
         "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
                    "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world} (batch-sharded, no collective)",
                    "l2": ("L2 flushed between steps (512 MB write outside the events)" if flush
