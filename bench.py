@@ -261,6 +261,77 @@ def run_reference(args, cfg_tuple, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_strong(args, cfg_tuple):
+    """Strong scaling in one process: the public ShardedTransformer splits
+    the batch over --gpus local GPUs (input handed over on cuda:0, shards
+    copied over NVLink, per-device graph replicas, outputs gathered back on
+    cuda:0). cuda:0's current stream waits on every device, so CUDA events
+    on it time the whole sharded forward (the max over devices)."""
+    import _tklib as tk
+    import optimized
+    import sharded
+
+    B, S, d, H, ffn, L, causal = cfg_tuple
+    n = args.gpus
+    if torch.cuda.device_count() < n:
+        raise SystemExit(f"--strong --gpus {n}: only {torch.cuda.device_count()} GPUs visible")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(0)
+    model = optimized.OptimizedTransformer(optimized.TransformerConfig(B, S, d, H, ffn, L, causal)).to(dev).eval()
+    shard = sharded.ShardedTransformer(model, [f"cuda:{i}" for i in range(n)])
+    gen = torch.Generator().manual_seed(1234 + 100000)
+    x_host = torch.randn(B, S, d, generator=gen).pin_memory()
+    mask = torch.ones(B, S, dtype=torch.bool, device=dev)
+    x = x_host.to(dev)
+    out_host = torch.empty(B, S, d, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    with torch.inference_mode():
+        import cuda_graphs
+        for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 1 + args.warmup):
+            shard(x, mask)
+        for i in range(n):
+            tk.check_device_errors(torch.device("cuda", i))
+        torch.cuda.synchronize(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(0) as clk:
+            clk.mark("t_start")
+            t0.record(stream)
+            for _ in range(args.steps):
+                shard(x, mask)
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
+            clk.mark("t_end")
+        ms = t0.elapsed_time(t1) / args.steps
+        # end to end: pinned host input -> cuda:0 -> sharded forward -> pinned host output
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            x.copy_(x_host, non_blocking=True)
+            out_host.copy_(shard(x, mask), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+        for i in range(n):
+            tk.check_device_errors(torch.device("cuda", i))
+    tokens = B * S
+    line = {
+        "metric": METRIC, "value": tokens * 1000.0 / ms, "unit": "tokens/s", "n_gpus": n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16 operands / f32 accumulate+residual", "data": "synthetic",
+        "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
+                   "global_batch": B, "seq_len": S,
+                   "parallelism": f"dp{n} in one process (batch split over {n} GPUs, NVLink scatter/gather)",
+                   "l2": "inputs and activations > 126 MB L2; no flush"},
+        "e2e": {"value": tokens * 1000.0 / e2e_ms, "unit": "tokens/s", "ms_per_step": e2e_ms,
+                "path": "pinned host -> cuda:0 -> ShardedTransformer -> pinned host",
+                "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 4},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def measured_traffic(config, kernel, batch):
     """DRAM bytes (read + write) per launch of `kernel` from the committed ncu
     summary profiles/dram_traffic.json, captured on a smaller batch of the
@@ -286,6 +357,9 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=4, help="batch slices of the streamed end-to-end forward")
+    ap.add_argument("--strong", action="store_true",
+                    help="one process drives --gpus local GPUs: the config's batch is split across them "
+                         "(ShardedTransformer, NVLink scatter/gather) -- strong scaling")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = DEFAULT_STEPS.get(args.config, 60)
@@ -305,6 +379,10 @@ def main() -> int:
     if args.impl == "reference":
         run_reference(args, cfg_tuple, rank)
         return 0
+    if args.strong:
+        if world > 1:
+            ap.error("--strong runs in one process; do not launch it under torchrun")
+        return run_strong(args, cfg_tuple)
 
     import torch.distributed as dist
     from datetime import timedelta
