@@ -517,6 +517,15 @@ def main() -> int:
         achieved = fl[dom] / (avg_ms * 1e-3) / 1e12
         roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
                 "frac": achieved / tf_sus, "peak_kind": f"{peak_kind} bf16 sustained"}
+    elif dom == "stack_small":
+        # the whole forward is one kernel: all GEMM and attention FLOP of the stack
+        g = gemm_flops(T, d, ffn)
+        total = L * (g["gemm_qkv"] + g["gemm_o"] + g["gemm_ffn_in"] + g["gemm_ffn_out"]
+                     + attn_flops(B, S, H, d // H, causal))
+        achieved = total / (avg_ms * 1e-3) / 1e12
+        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
+                "frac": achieved / tf_sus, "peak_kind": f"{peak_kind} bf16 sustained",
+                "note": "one-launch whole-stack kernel; latency-bound at this size"}
     elif dom == "attn":
         achieved = attn_flops(B, S, H, d // H, causal) / (avg_ms * 1e-3) / 1e12
         roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",

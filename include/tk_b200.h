@@ -108,6 +108,30 @@ TK_API int tk_attn_fwd(const void* q, const void* k, const void* v,
                 int64_t B, int64_t S, int64_t H, int64_t hd, float scale,
                 int causal, const int32_t* kv_len, void* stream);
 
+/* Whole-stack forward for small shapes, one launch: every layer of the
+ * stack for one sequence per CTA (d_model = ffn = 128, 2 or 4 heads,
+ * S <= 128; the harness's case 1 and the appendix shapes around it).
+ * Replaces, for those shapes, the whole per-layer sequence that
+ * OptimizedTransformer._run_layers_fused (src/optimized.py:488-554) runs
+ * kernel by kernel. Inputs:
+ *   x, out       : fp32 [B, S, 128], contiguous
+ *   w_packed     : fp16 [L * 768, 128] -- per layer the rows of Wq, Wk, Wv
+ *                  (384), Wo, W_ffn_in, W_ffn_out (128 each), nn.Linear
+ *                  layout [out, in]
+ *   vec_packed   : fp32 [L, 1280] -- per layer bq|bk|bv (384), bo, b_in,
+ *                  b_out, norm1 weight, norm1 bias, norm2 weight, norm2 bias
+ *   final_gamma/beta : fp32 [128]; eps: every LayerNorm's epsilon
+ *   row_len      : optional int32 [B] prefix lengths (key padding; padded
+ *                  rows are zero in the output)
+ *   scale        : attention scale (head_dim**-0.5)
+ * Same numerics as the layer-by-layer path (fp16 operands, fp32
+ * accumulation, residual stream and statistics). */
+TK_API int tk_stack_small_supported(int64_t d, int64_t heads, int64_t ffn, int64_t seq_len);
+TK_API int tk_stack_small(const float* x, float* out, const void* w_packed, const float* vec_packed,
+                          const float* final_gamma, const float* final_beta, float eps,
+                          const int32_t* row_len, int64_t B, int64_t S, int64_t d, int64_t heads,
+                          int64_t ffn, int64_t L, int causal, float scale, void* stream);
+
 /* Guard probes, same meaning as the reference's can_fuse
  * (src/fused_kernels.py:62-64) and attention_supported
  * (src/kernels.py:96-103): 1 when the kernels accept the shape. */

@@ -191,3 +191,29 @@ def test_appendix6_batch_10000_spot_sequences(cuda_device):
     ref = stack_forward(params, sub, x[pick], mask[pick])
     r = compare_outputs(ref, out[pick], RTOL, ATOL)
     assert r.passed, str(r)
+
+
+# The one-launch whole-stack kernel (d = ffn = 128, 2 or 4 heads, S <= 128):
+# C1 itself, appendix case 12 (S = 32), a bidirectional 2-head stack with a
+# ragged S, a one-token sequence; dense and padded prefix masks.
+SMALL_STACK = [StackConfig(8, 128, 128, 4, 128, 4, True), StackConfig(8, 32, 128, 4, 128, 4, True),
+               StackConfig(4, 77, 128, 2, 128, 3, False), StackConfig(3, 1, 128, 4, 128, 2, True)]
+
+
+@pytest.mark.parametrize("cfg", SMALL_STACK, ids=lambda c: f"b{c.batch_size}s{c.seq_len}h{c.num_heads}")
+@pytest.mark.parametrize("padding", [0.0, 0.3])
+def test_small_stack_kernel(cuda_device, cfg, padding):
+    params, model = build(cfg)
+    model.launch_trace = []
+    x, mask = generate_random_case(cfg, 1240, padding)
+    ref = stack_forward(params, cfg, x, mask)
+    with torch.inference_mode():
+        out = model(x.cuda(), mask.cuda()).cpu()
+    assert [name for name, _, _ in model.launch_trace] == ["stack_small"]
+    r = compare_outputs(ref, out, RTOL, ATOL)
+    assert r.passed, str(r)
+    # same result as the per-layer kernel sequence, to within the fp16 rounding of either path
+    _, per_layer = build(cfg, fused_small_stack=False)
+    with torch.inference_mode():
+        out2 = per_layer(x.cuda(), mask.cuda()).cpu()
+    torch.testing.assert_close(out, out2, atol=2e-3, rtol=2e-2)

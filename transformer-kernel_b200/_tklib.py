@@ -43,6 +43,8 @@ SIGNATURES = {
     "tk_check_device_errors": (_I, [_P]),
     "tk_set_wait_limit_ns": (_U64, [_U64]),
     "tk_set_programmatic_launch": (_I, [_I]),
+    "tk_stack_small_supported": (_I, [_I64, _I64, _I64, _I64]),
+    "tk_stack_small": (_I, [_P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _F, _P]),
     "tk_selftest_wait_timeout": (_I, [_P]),
     "tk_last_error": (ctypes.c_char_p, []),
     "tk_version": (ctypes.c_char_p, []),

@@ -15,6 +15,7 @@
 #include "tk_attn_wide.cuh"
 #include "tk_gemm.cuh"
 #include "tk_layernorm.cuh"
+#include "tk_stack_small.cuh"
 #include "tk_ptx.cuh"
 #include "../../include/tk_b200.h"
 
@@ -108,6 +109,7 @@ struct DeviceInfo {
   int sms = 0;
   bool gemm_attr_set[4][4] = {};
   bool attn_attr_set[5] = {};
+  bool small_attr_set[2] = {};
 };
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
@@ -395,6 +397,70 @@ int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
     case 256: return launch_gemm_epi<256>(epilogue, ma, mw, p, info, s);
   }
   return fail(TK_ERR_UNSUPPORTED, "tk_gemm: no kernel for tile width %d", bn);
+}
+
+int tk_stack_small_supported(int64_t d, int64_t heads, int64_t ffn, int64_t seq_len) {
+  return d == 128 && ffn == 128 && (heads == 2 || heads == 4) && seq_len >= 1 && seq_len <= 128 ? 1 : 0;
+}
+
+int tk_stack_small(const float* x, float* out, const void* w_packed, const float* vec_packed, const float* final_gamma,
+                   const float* final_beta, float eps, const int32_t* row_len, int64_t B, int64_t S, int64_t d,
+                   int64_t heads, int64_t ffn, int64_t L, int causal, float scale, void* stream) {
+  g_last_error.clear();
+  if (x == nullptr || out == nullptr || w_packed == nullptr || vec_packed == nullptr || final_gamma == nullptr ||
+      final_beta == nullptr)
+    return fail(TK_ERR_INVALID, "tk_stack_small: null pointer");
+  if (B < 0 || L < 1) return fail(TK_ERR_INVALID, "tk_stack_small: B=%lld L=%lld", (long long)B, (long long)L);
+  if (!tk_stack_small_supported(d, heads, ffn, S))
+    return fail(TK_ERR_UNSUPPORTED, "tk_stack_small: needs d = ffn = 128, 2 or 4 heads, 1 <= S <= 128 (d=%lld "
+                "heads=%lld ffn=%lld S=%lld)", (long long)d, (long long)heads, (long long)ffn, (long long)S);
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(w_packed, 16) || !aligned(vec_packed, 16))
+    return fail(TK_ERR_INVALID, "tk_stack_small: x / out / packed weights need 16-byte alignment");
+  if (B > (1ll << 31) - 1 || L * tk::small::kWRowsPerLayer > (1ll << 31) - 1)
+    return fail(TK_ERR_UNSUPPORTED, "tk_stack_small: too large");
+  if (B == 0) return TK_OK;
+  int dev;
+  DeviceInfo* info;
+  if (int st = current_device(&dev, &info)) return st;
+  CUtensorMap mw;
+  {
+    cuuint64_t dims[2] = {128, static_cast<cuuint64_t>(L * tk::small::kWRowsPerLayer)};
+    cuuint64_t strides[1] = {256};
+    cuuint32_t box[2] = {64, 128};
+    if (int st = make_map_f16(&mw, w_packed, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  tk::small::Params p;
+  p.x = x;
+  p.out = out;
+  p.vec = vec_packed;
+  p.final_g = final_gamma;
+  p.final_b = final_beta;
+  p.row_len = row_len;
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.H = static_cast<int>(heads);
+  p.L = static_cast<int>(L);
+  p.causal = causal ? 1 : 0;
+  p.eps = eps;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.wait_limit_ns = g_wait_limit_ns.load();
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto run = [&](auto kern, int slot, int smem_bytes) -> cudaError_t {
+    {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      if (!info->small_attr_set[slot]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+        if (e != cudaSuccess) return e;
+        info->small_attr_set[slot] = true;
+      }
+    }
+    return launch(kern, dim3(static_cast<unsigned>(B)), dim3(tk::small::kThreads), smem_bytes, s, true, mw, p);
+  };
+  cudaError_t e = heads == 4 ? run(tk::small::stack_small_kernel<32>, 0, tk::small::Cfg<32>::SMEM_BYTES)
+                             : run(tk::small::stack_small_kernel<64>, 1, tk::small::Cfg<64>::SMEM_BYTES);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tk_stack_small launch");
+  return TK_OK;
 }
 
 int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, int64_t stride_h, int64_t stride_s,

@@ -73,6 +73,11 @@ class OptimizerSettings:
     # Synchronise after every forward and raise if a kernel's bounded
     # device-side wait gave up (debugging aid; costs a sync per call).
     check_device_errors: bool = False
+    # Run shapes the one-launch whole-stack kernel takes (d_model = ffn =
+    # 128, 2 or 4 heads, seq_len <= 128, equal LayerNorm eps) through it
+    # instead of the per-layer kernel sequence (the reference's shape
+    # dispatch picks per-shape paths the same way, src/dispatch.py:95-172).
+    fused_small_stack: bool = True
 
 
 _ACTIVE = OptimizerSettings()
@@ -189,8 +194,25 @@ class OptimizedTransformer(nn.Module):
                     )
                 )
         self._final = (f32(self.final_norm.weight), f32(self.final_norm.bias), self.final_norm.eps)
+        self._small_pack = None  # packed weights of the one-launch small-shape kernel, built on first use
         self._weight_cache, self._weight_cache_key = built, key
         return built
+
+    def _small_stack_pack(self, weights: List[_LayerWeights]):
+        """(w fp16 [L*768, 128], vec fp32 [L, 1280], eps) for tk_stack_small,
+        or None when the LayerNorm epsilons differ (the kernel takes one)."""
+        if self._small_pack is not None:
+            return self._small_pack
+        eps = {w.norm1_eps for w in weights} | {w.norm2_eps for w in weights} | {self._final[2]}
+        if len(eps) != 1:
+            self._small_pack = False
+            return None
+        with torch.no_grad():
+            w = torch.cat([torch.cat([lw.qkv_w, lw.out_w, lw.ffn_in_w, lw.ffn_out_w], 0) for lw in weights], 0)
+            vec = torch.stack([torch.cat([lw.qkv_b, lw.out_b, lw.ffn_in_b, lw.ffn_out_b, lw.norm1_w, lw.norm1_b,
+                                          lw.norm2_w, lw.norm2_b]) for lw in weights], 0)
+        self._small_pack = (w.contiguous(), vec.contiguous(), float(eps.pop()))
+        return self._small_pack
 
     @_outside_compile
     def _prefix_lengths(self, mask: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
@@ -259,11 +281,52 @@ class OptimizedTransformer(nn.Module):
         self._pinned_activations = ((B, S, d, ffn, x.device), bufs)
         return bufs
 
+    def _small_stack(self, x, lengths, out, weights) -> Optional[torch.Tensor]:
+        """The whole forward in one tk_stack_small launch when the shape and
+        settings allow it; None otherwise."""
+        B, S, d = x.shape
+        ffn = weights[0].ffn_in_w.shape[0]
+        if not (self.settings.fused_small_stack and
+                tk.lib().tk_stack_small_supported(d, self.num_heads, ffn, S)):
+            return None
+        pack = self._small_stack_pack(weights)
+        if not pack:
+            return None
+        w, vec, eps = pack
+        xin = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.to(torch.float32).contiguous()
+        if out is None:
+            pinned = getattr(self, "_pinned_activations", None)
+            if pinned is not None and pinned[0] == (B, S, d, ffn, x.device):
+                out = pinned[1][5]  # graph capture: the output buffer was allocated before capture
+            else:
+                out = torch.empty((B, S, d), dtype=torch.float32, device=x.device)
+        fg, fb, _ = self._final
+        run = (lambda fn: fn()) if self.launch_trace is None else self._traced("stack_small")
+        run(lambda: tk.call(
+            "tk_stack_small", xin.data_ptr(), out.data_ptr(), w.data_ptr(), vec.data_ptr(), fg.data_ptr(),
+            fb.data_ptr(), eps, tk.ptr(lengths), B, S, d, self.num_heads, ffn, len(weights),
+            1 if self.config.causal else 0, self.attn_scale, tk.stream_handle(x.device)))
+        return out.view(B, S, d)
+
+    def _traced(self, name):
+        def wrap(fn):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            result = fn()
+            end.record()
+            self.launch_trace.append((name, start, end))
+            return result
+        return wrap
+
     def _run(self, x: torch.Tensor, lengths: Optional[torch.Tensor], out: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, S, d = x.shape
         T = B * S
         dev = x.device
         weights = self._weights()
+        with torch.cuda.device(dev):
+            fused = self._small_stack(x, lengths, out, weights)
+        if fused is not None:
+            return fused
         ffn = weights[0].ffn_in_w.shape[0]
         hd = self.head_dim
         fused = self.settings.fused_ln_epilogue and tk_linear.fused_ln_supported(d)
