@@ -107,16 +107,17 @@ __device__ __forceinline__ void tmem_store_chunk(uint32_t t, const float (&v)[32
 // statistics, 32 columns at a time: the loops stay rolled, so the kernel's
 // code stays small enough for the instruction cache).
 __device__ __forceinline__ void row_stats(uint32_t t, float eps, float& mean, float& rstd) {
-  float s = 0.f;
+  // four partial sums per pass: short dependency chains
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
   for (int q = 0; q < 4; ++q) {
     float v[32];
     tmem_chunk(t + q * 32, v);
 #pragma unroll
-    for (int k = 0; k < 32; ++k) s += v[k];
+    for (int k = 0; k < 32; ++k) s4[k & 3] += v[k];
   }
-  mean = s * (1.f / kD);
-  float var = 0.f;
+  mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / kD);
+  float v4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
   for (int q = 0; q < 4; ++q) {
     float v[32];
@@ -124,10 +125,10 @@ __device__ __forceinline__ void row_stats(uint32_t t, float eps, float& mean, fl
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
       const float d = v[k] - mean;
-      var += d * d;
+      v4[k & 3] = fmaf(d, d, v4[k & 3]);
     }
   }
-  rstd = rsqrtf(var * (1.f / kD) + eps);
+  rstd = rsqrtf(((v4[0] + v4[1]) + (v4[2] + v4[3])) * (1.f / kD) + eps);
 }
 
 // LayerNorm of the 128 values in TMEM at t into row r of the A operand tile
@@ -458,18 +459,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t t_s = t_lane + kColAcc + b * 128;
         // pass 1: row max over the valid keys
-        float mx = -INFINITY;
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
           float v[32];
           tmem_chunk(t_s + q * 32, v);
 #pragma unroll
-          for (int k = 0; k < 32; ++k)
-            if (q * 32 + k < lim) mx = fmaxf(mx, v[k]);
+          for (int k = 0; k < 32; ++k) mx4[k & 3] = fmaxf(mx4[k & 3], q * 32 + k < lim ? v[k] : -INFINITY);
         }
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         const float neg_mc = (mx == -INFINITY) ? 0.f : -mx * sl;
         // pass 2: P = 2^(s*c - m*c), packed fp16 over the scores already read
-        float lsum = 0.f;
+        float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
           float v[32];
@@ -480,11 +481,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int c = q * 32 + k;
             const float e0 = (c < lim) ? ex2_approx(fmaf(v[k], sl, neg_mc)) : 0.f;
             const float e1 = (c + 1 < lim) ? ex2_approx(fmaf(v[k + 1], sl, neg_mc)) : 0.f;
-            lsum += e0 + e1;
+            ls4[(k >> 1) & 3] += e0 + e1;
             w[k / 2] = pack_half2(e0, e1);
           }
           tmem_st16(t_s + q * 16, w);
         }
+        const float lsum = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
         inv_l_sh[h][r] = lsum > 0.f ? 1.f / lsum : 0.f;
         tmem_st_wait();
         signal(&p_full);
