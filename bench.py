@@ -68,6 +68,18 @@ CONFIGS = {
 # results/pass2-default.json); A14 is appendix case 14 (155.4 s per forward,
 # 20,597 tokens/s, results/case14-full.json). No other config was published.
 PUBLISHED_TOKENS_PER_S = {"C1": 5.83e6, "A14": 20597.0}
+# The reference's appendix shapes (configs/shapes.json; every case causal):
+# case: (B, S, d, H, ffn, L), with its best published T4 time in ms
+# (README.md:298-312 pass two; case 14: README.md:401-405).
+APPENDIX = {
+    1: ((64, 128, 128, 4, 128, 4), 1.42), 2: ((1, 128, 128, 4, 128, 4), 0.30),
+    3: ((4, 128, 128, 4, 128, 4), 0.31), 4: ((16, 128, 128, 4, 128, 4), 0.43),
+    5: ((128, 128, 128, 4, 128, 4), 2.66), 6: ((10000, 128, 128, 4, 128, 4), 198.57),
+    7: ((64, 128, 32, 4, 32, 4), 1.60), 8: ((64, 128, 1024, 4, 1024, 4), 25.23),
+    9: ((64, 128, 128, 1, 128, 4), 1.43), 10: ((64, 128, 128, 2, 128, 4), 1.50),
+    11: ((64, 128, 128, 16, 128, 4), 2.18), 12: ((64, 32, 128, 4, 128, 4), 0.42),
+    13: ((64, 1024, 128, 4, 128, 4), 18.75), 14: ((32, 100000, 1024, 16, 1024, 2), 155400.0),
+}
 # timed steps when --steps is not given (C5: ~1 s per forward on one GPU)
 DEFAULT_STEPS = {"C5": 3, "A14": 3}
 # configurations whose working set fits in the 126 MB L2: flush it between steps
@@ -261,6 +273,57 @@ def run_reference(args, cfg_tuple, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_sweep(args):
+    """Appendix-shape sweep on one GPU (the reference's src/sweep.py runs the
+    same 14 shapes through its harness): per case, the public drop-in
+    (graph-replayed when a forward is short), warm-up, then the median of
+    per-forward CUDA-event samples with an L2 flush between samples; one JSON
+    line per case with the reference's best published T4 time beside it."""
+    import _tklib as tk
+    import cuda_graphs
+    import optimized
+
+    cases = sorted(APPENDIX) if args.sweep == "all" else [int(c) for c in args.sweep.split(",")]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    scratch = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for case in cases:
+        (B, S, d, H, ffn, L), t4_ms = APPENDIX[case]
+        cfg = optimized.TransformerConfig(B, S, d, H, ffn, L, True)
+        torch.manual_seed(0)
+        big = B * S >= 1_000_000
+        model = (optimized.OptimizedTransformer(cfg) if big else cuda_graphs.GraphedTransformer(cfg)).to(dev).eval()
+        gen = torch.Generator().manual_seed(1234 + 100000)
+        x = torch.randn(B, S, d, generator=gen).to(dev)
+        mask = torch.ones(B, S, dtype=torch.bool, device=dev)
+        samples = []
+        with torch.inference_mode():
+            for _ in range((0 if big else cuda_graphs.WARMUP_BEFORE_CAPTURE + 1) + 3):
+                model(x, mask)
+            torch.cuda.synchronize(dev)
+            n = 3 if big else (args.steps if args.steps else 30)
+            for _ in range(n):
+                scratch.fill_(1)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                model(x, mask)
+                b.record(stream)
+                samples.append((a, b))
+            torch.cuda.synchronize(dev)
+        ms = statistics.median(a.elapsed_time(b) for a, b in samples)
+        line = {"case": case, "shape": {"batch": B, "seq": S, "d_model": d, "heads": H, "ffn": ffn, "layers": L,
+                                        "causal": True},
+                "ms": ms, "tokens_per_s": B * S * 1000.0 / ms, "samples": n,
+                "reference_t4_ms": t4_ms, "speedup_vs_reference_t4": t4_ms / ms,
+                "path": ("one-launch stack kernel" if model.settings.fused_small_stack
+                         and tk.lib().tk_stack_small_supported(d, H, ffn, S) else "per-layer kernels")}
+        print(json.dumps(line), flush=True)
+        del model, x
+        torch.cuda.empty_cache()
+    return 0
+
+
 def run_strong(args, cfg_tuple):
     """Strong scaling in one process: the public ShardedTransformer splits
     the batch over --gpus local GPUs (input handed over on cuda:0, shards
@@ -357,6 +420,8 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=4, help="batch slices of the streamed end-to-end forward")
+    ap.add_argument("--sweep", default="", help="comma-separated appendix cases (or 'all'): one JSON line each, "
+                                                "timed like the harness (median of CUDA-event samples)")
     ap.add_argument("--strong", action="store_true",
                     help="one process drives --gpus local GPUs: the config's batch is split across them "
                          "(ShardedTransformer, NVLink scatter/gather) -- strong scaling")
@@ -379,6 +444,8 @@ def main() -> int:
     if args.impl == "reference":
         run_reference(args, cfg_tuple, rank)
         return 0
+    if args.sweep:
+        return run_sweep(args)
     if args.strong:
         if world > 1:
             ap.error("--strong runs in one process; do not launch it under torchrun")

@@ -83,6 +83,10 @@ __device__ __forceinline__ uint32_t swz_unit(int r, int u, int units) {
   return units == 8 ? (u ^ (r & 7)) : (u ^ ((r >> 1) & 3));
 }
 
+// Four consecutive fp32 parameters (bias, LayerNorm affine) through the
+// read-only path; every thread of the CTA reads the same addresses.
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
 // 32 fp32 values of this thread's TMEM lane from column t.
 __device__ __forceinline__ void tmem_chunk(uint32_t t, float (&v)[32]) {
   uint32_t r[32];
@@ -143,13 +147,16 @@ __device__ __forceinline__ void ln_tmem_to_a(uint32_t t, const float* g, const f
     tmem_chunk(t + q * 32, v);
 #pragma unroll
     for (int u4 = 0; u4 < 4; ++u4) {
+      const int c8 = q * 32 + u4 * 8;
+      const float4 g0 = ldg4(g + c8), g1 = ldg4(g + c8 + 4), b0 = ldg4(b + c8), b1 = ldg4(b + c8 + 4);
+      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
       uint32_t w[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const int cl = u4 * 8 + 2 * k;
-        const int c = q * 32 + cl;
-        w[k] = pack_half2((v[cl] - mean) * rstd * __ldg(g + c) + __ldg(b + c),
-                          (v[cl + 1] - mean) * rstd * __ldg(g + c + 1) + __ldg(b + c + 1));
+        w[k] = pack_half2((v[cl] - mean) * rstd * gg[2 * k] + bb[2 * k],
+                          (v[cl + 1] - mean) * rstd * gg[2 * k + 1] + bb[2 * k + 1]);
       }
       const int u = q * 4 + u4;
       uint8_t* atom = sA + (u >> 3) * kAtomBytes;
@@ -165,8 +172,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int H = C::H;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t w_full[2], w_empty[2];
-  __shared__ __align__(8) uint64_t a_ready, acc_full, qkv_ready, p_full, attn_done, pv_bar, drain_bar;
-  __shared__ __align__(8) uint64_t s_full[2];
+  __shared__ __align__(8) uint64_t a_ready, acc_full, qkv_ready, attn_done, pv_bar, drain_bar;
+  // Per score buffer (head parity): scores ready / P stored. One barrier per
+  // buffer, so a warp that finishes head h early and moves on to head h+1
+  // arrives on the other barrier and cannot complete head h's phase.
+  __shared__ __align__(8) uint64_t s_full[2], p_full[2];
   __shared__ float inv_l_sh[4][kRows];  // per head, per row: 1 / softmax row sum
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -187,11 +197,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&w_full[s], 1);
       mbar_init(&w_empty[s], 1);
       mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 4);
     }
     mbar_init(&a_ready, 4);
     mbar_init(&acc_full, 1);
     mbar_init(&qkv_ready, 4);
-    mbar_init(&p_full, 4);
     mbar_init(&attn_done, 1);
     mbar_init(&pv_bar, 1);
     mbar_init(&drain_bar, 1);
@@ -242,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_g = idesc_f16_f32(kRows, 128, false, false);  // GEMM n-tile / scores
       constexpr uint32_t idesc_o = idesc_f16_f32(kRows, HD, false, true);    // P V (V MN-major)
-      int nw = 0, na = 0, np = 0, npv = 0;
+      int nw = 0, na = 0, npv = 0, np0 = 0, np1 = 0;
       bool ok = true;
       auto fail = [&](unsigned site) {
         report_error(kDevWaitTimeout, kid * 256 + site);
@@ -298,11 +308,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         issue_s(0);
         if (H > 1) issue_s(1);
         for (int h = 0; h < H && ok; ++h) {
-          if (!mbar_wait(&p_full, np & 1, &abort_flag, p.wait_limit_ns)) {
+          const uint32_t p_phase = (h & 1) == 0 ? (np0++ & 1) : (np1++ & 1);
+          if (!mbar_wait(&p_full[h & 1], p_phase, &abort_flag, p.wait_limit_ns)) {
             fail(kSiteP);
             break;
           }
-          ++np;
           tc_fence_after();
           const uint32_t v_addr = smem_u32(sV + h * C::HEAD_TILE);
           const uint32_t p_col = kColAcc + (h & 1) * 128;  // P over the first 64 score columns
@@ -403,9 +413,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_chunk(t_x + q * 32, v);
         tmem_chunk(t_lane + kColAcc + q * 32, a);
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float y = keep ? v[k] : v[k] + (a[k] + __ldg(bias + q * 32 + k));
-          v[k] = zero ? 0.f : y;
+        for (int k4 = 0; k4 < 8; ++k4) {
+          const float4 bq = ldg4(bias + q * 32 + 4 * k4);
+          const float bb[4] = {bq.x, bq.y, bq.z, bq.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int k = 4 * k4 + j;
+            const float y = keep ? v[k] : v[k] + (a[k] + bb[j]);
+            v[k] = zero ? 0.f : y;
+          }
         }
         tmem_store_chunk(t_x + q * 32, v);
       }
@@ -429,13 +445,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* tile = dst + hh * C::HEAD_TILE + r * C::ROW_BYTES;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
+            const int g8 = t * 128 + q * 32 + u * 8;
+            const float4 bq0 = ldg4(vec + g8), bq1 = ldg4(vec + g8 + 4);
+            const float bb[8] = {bq0.x, bq0.y, bq0.z, bq0.w, bq1.x, bq1.y, bq1.z, bq1.w};
             uint32_t w[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int c = u * 8 + 2 * k;
-              const int gc = t * 128 + q * 32 + c;
-              w[k] = pack_half2(__uint_as_float(raw[c]) + __ldg(vec + gc),
-                                __uint_as_float(raw[c + 1]) + __ldg(vec + gc + 1));
+              w[k] = pack_half2(__uint_as_float(raw[c]) + bb[2 * k], __uint_as_float(raw[c + 1]) + bb[2 * k + 1]);
             }
             const int unit = c0 / 8 + u;
             *reinterpret_cast<uint4*>(tile + swz_unit(r, unit, C::ROW_BYTES / 16) * 16) =
@@ -448,6 +465,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int lim = len;  // keys < lim are valid
       if (p.causal) lim = min(lim, r + 1);
       const float sl = p.scale_log2;
+      // 32-key chunks with any valid key for some row of this warp (rows
+      // 32*quad .. 32*quad+31): the rest are skipped and their P written as 0.
+      int q_end = (len + 31) / 32;
+      if (p.causal) q_end = min(q_end, quad + 1);
 #pragma unroll 1
       for (int h = 0; h < H && ok; ++h) {
         const int b = h & 1;
@@ -461,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // pass 1: row max over the valid keys
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < q_end; ++q) {
           float v[32];
           tmem_chunk(t_s + q * 32, v);
 #pragma unroll
@@ -472,7 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // pass 2: P = 2^(s*c - m*c), packed fp16 over the scores already read
         float ls4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < q_end; ++q) {
           float v[32];
           tmem_chunk(t_s + q * 32, v);
           uint32_t w[16];
@@ -486,10 +507,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_st16(t_s + q * 16, w);
         }
+#pragma unroll 1
+        for (int q = q_end; q < 4; ++q) {
+          uint32_t w[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) w[k] = 0u;
+          tmem_st16(t_s + q * 16, w);
+        }
         const float lsum = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
         inv_l_sh[h][r] = lsum > 0.f ? 1.f / lsum : 0.f;
         tmem_st_wait();
-        signal(&p_full);
+        signal(&p_full[b]);
       }
       if (!ok) break;
       if (!mbar_wait(&attn_done, l & 1, &abort_flag, p.wait_limit_ns)) {
@@ -531,13 +559,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_chunk(t_lane + kColAcc + q * 32, a);
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
+          const int c8 = q * 32 + u4 * 8;
+          const float4 c0 = ldg4(vec + 512 + c8), c1 = ldg4(vec + 516 + c8);
+          const float bb[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
           uint32_t w[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int cl = u4 * 8 + 2 * k;
-            const int c = q * 32 + cl;
-            const float2 gl =
-                gemm::gelu_erf2(make_float2(a[cl] + __ldg(vec + 512 + c), a[cl + 1] + __ldg(vec + 513 + c)));
+            const float2 gl = gemm::gelu_erf2(make_float2(a[cl] + bb[2 * k], a[cl + 1] + bb[2 * k + 1]));
             w[k] = pack_half2(gl.x, gl.y);
           }
           const int u = q * 4 + u4;
@@ -568,10 +597,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 8; ++c) {
             float4 o;
             const int gc = q * 32 + 4 * c;
-            o.x = (v[4 * c] - mean) * rstd * __ldg(p.final_g + gc) + __ldg(p.final_b + gc);
-            o.y = (v[4 * c + 1] - mean) * rstd * __ldg(p.final_g + gc + 1) + __ldg(p.final_b + gc + 1);
-            o.z = (v[4 * c + 2] - mean) * rstd * __ldg(p.final_g + gc + 2) + __ldg(p.final_b + gc + 2);
-            o.w = (v[4 * c + 3] - mean) * rstd * __ldg(p.final_g + gc + 3) + __ldg(p.final_b + gc + 3);
+            const float4 fg = ldg4(p.final_g + gc), fb = ldg4(p.final_b + gc);
+            o.x = (v[4 * c] - mean) * rstd * fg.x + fb.x;
+            o.y = (v[4 * c + 1] - mean) * rstd * fg.y + fb.y;
+            o.z = (v[4 * c + 2] - mean) * rstd * fg.z + fb.z;
+            o.w = (v[4 * c + 3] - mean) * rstd * fg.w + fb.w;
             if (row_pad) o = make_float4(0.f, 0.f, 0.f, 0.f);
             if (row_valid) dst[c] = o;
           }
