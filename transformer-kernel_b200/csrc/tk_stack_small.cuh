@@ -107,31 +107,49 @@ __device__ __forceinline__ void tmem_store_chunk(uint32_t t, const float (&v)[32
   tmem_st16(t + 16, hi);
 }
 
+// body(v, q) for the 32-column TMEM chunks q = 0..n-1 at addr(q), with the
+// load of chunk q+1 in flight while chunk q is processed. tcgen05.wait::ld
+// waits for all of a thread's loads, so the loop alternates two register
+// buffers. n must be warp-uniform.
+template <typename Addr, typename Body>
+__device__ __forceinline__ void tmem_pipeline(int n, Addr addr, Body body) {
+  if (n <= 0) return;
+  uint32_t a[32], b[32];
+  tmem_ld32(addr(0), a);
+  tmem_ld_wait(a);
+#pragma unroll 1
+  for (int q = 0; q < n; q += 2) {
+    if (q + 1 < n) tmem_ld32(addr(q + 1), b);
+    body(a, q);
+    if (q + 1 < n) {
+      tmem_ld_wait(b);
+      if (q + 2 < n) tmem_ld32(addr(q + 2), a);
+      body(b, q + 1);
+      if (q + 2 < n) tmem_ld_wait(a);
+    }
+  }
+}
+
 // Mean and 1/sqrt(var + eps) of the 128 values in TMEM at t (two-pass fp32
 // statistics, 32 columns at a time: the loops stay rolled, so the kernel's
 // code stays small enough for the instruction cache).
 __device__ __forceinline__ void row_stats(uint32_t t, float eps, float& mean, float& rstd) {
   // four partial sums per pass: short dependency chains
+  auto col = [t](int q) { return t + q * 32; };
   float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int q = 0; q < 4; ++q) {
-    float v[32];
-    tmem_chunk(t + q * 32, v);
+  tmem_pipeline(4, col, [&](uint32_t(&v)[32], int) {
 #pragma unroll
-    for (int k = 0; k < 32; ++k) s4[k & 3] += v[k];
-  }
+    for (int k = 0; k < 32; ++k) s4[k & 3] += __uint_as_float(v[k]);
+  });
   mean = ((s4[0] + s4[1]) + (s4[2] + s4[3])) * (1.f / kD);
   float v4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int q = 0; q < 4; ++q) {
-    float v[32];
-    tmem_chunk(t + q * 32, v);
+  tmem_pipeline(4, col, [&](uint32_t(&v)[32], int) {
 #pragma unroll
     for (int k = 0; k < 32; ++k) {
-      const float d = v[k] - mean;
+      const float d = __uint_as_float(v[k]) - mean;
       v4[k & 3] = fmaf(d, d, v4[k & 3]);
     }
-  }
+  });
   rstd = rsqrtf(((v4[0] + v4[1]) + (v4[2] + v4[3])) * (1.f / kD) + eps);
 }
 
@@ -141,10 +159,10 @@ __device__ __forceinline__ void ln_tmem_to_a(uint32_t t, const float* g, const f
                                              int r) {
   float mean, rstd;
   row_stats(t, eps, mean, rstd);
-#pragma unroll 1
-  for (int q = 0; q < 4; ++q) {
+  tmem_pipeline(4, [t](int q) { return t + q * 32; }, [&](uint32_t(&raw)[32], int q) {
     float v[32];
-    tmem_chunk(t + q * 32, v);
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(raw[k]);
 #pragma unroll
     for (int u4 = 0; u4 < 4; ++u4) {
       const int c8 = q * 32 + u4 * 8;
@@ -162,7 +180,7 @@ __device__ __forceinline__ void ln_tmem_to_a(uint32_t t, const float* g, const f
       uint8_t* atom = sA + (u >> 3) * kAtomBytes;
       *reinterpret_cast<uint4*>(atom + r * 128 + swz_unit(r, u & 7, 8) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
     }
-  }
+  });
 }
 
 template <int HD>
@@ -431,35 +449,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float* vec = p.vec + static_cast<int64_t>(l) * kVecPerLayer;
       // ---- q | k | v: + bias, fp16, into the per-head tiles ----
       if (!wait_acc()) break;
-#pragma unroll 1
-      for (int t = 0; t < 3; ++t) {
+      // the 12 chunks of the q | k | v accumulators are contiguous in TMEM
+      tmem_pipeline(12, [&](int i) { return t_lane + kColAcc + i * 32; }, [&](uint32_t(&raw)[32], int i) {
+        const int t = i >> 2, q = i & 3;
         uint8_t* dst = t == 0 ? sQ : t == 1 ? sK : sV;
-#pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
-          uint32_t raw[32];
-          tmem_ld32(t_lane + kColAcc + t * 128 + q * 32, raw);
-          tmem_ld_wait(raw);
-          // 32 columns = part of one head: head (q*32)/HD, columns from (q*32)%HD
-          const int hh = (q * 32) / HD;
-          const int c0 = (q * 32) % HD;
-          uint8_t* tile = dst + hh * C::HEAD_TILE + r * C::ROW_BYTES;
+        // 32 columns = part of one head: head (q*32)/HD, columns from (q*32)%HD
+        const int hh = (q * 32) / HD;
+        const int c0 = (q * 32) % HD;
+        uint8_t* tile = dst + hh * C::HEAD_TILE + r * C::ROW_BYTES;
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int g8 = t * 128 + q * 32 + u * 8;
-            const float4 bq0 = ldg4(vec + g8), bq1 = ldg4(vec + g8 + 4);
-            const float bb[8] = {bq0.x, bq0.y, bq0.z, bq0.w, bq1.x, bq1.y, bq1.z, bq1.w};
-            uint32_t w[4];
+        for (int u = 0; u < 4; ++u) {
+          const int g8 = i * 32 + u * 8;
+          const float4 bq0 = ldg4(vec + g8), bq1 = ldg4(vec + g8 + 4);
+          const float bb[8] = {bq0.x, bq0.y, bq0.z, bq0.w, bq1.x, bq1.y, bq1.z, bq1.w};
+          uint32_t w[4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int c = u * 8 + 2 * k;
-              w[k] = pack_half2(__uint_as_float(raw[c]) + bb[2 * k], __uint_as_float(raw[c + 1]) + bb[2 * k + 1]);
-            }
-            const int unit = c0 / 8 + u;
-            *reinterpret_cast<uint4*>(tile + swz_unit(r, unit, C::ROW_BYTES / 16) * 16) =
-                make_uint4(w[0], w[1], w[2], w[3]);
+          for (int k = 0; k < 4; ++k) {
+            const int c = u * 8 + 2 * k;
+            w[k] = pack_half2(__uint_as_float(raw[c]) + bb[2 * k], __uint_as_float(raw[c + 1]) + bb[2 * k + 1]);
           }
+          const int unit = c0 / 8 + u;
+          *reinterpret_cast<uint4*>(tile + swz_unit(r, unit, C::ROW_BYTES / 16) * 16) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
-      }
+      });
       signal(&qkv_ready);
       // ---- attention: one query row per thread; the key row (S <= 128) in one tile ----
       int lim = len;  // keys < lim are valid
@@ -481,32 +494,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t t_s = t_lane + kColAcc + b * 128;
         // pass 1: row max over the valid keys
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-        for (int q = 0; q < q_end; ++q) {
-          float v[32];
-          tmem_chunk(t_s + q * 32, v);
+        auto s_col = [t_s](int q) { return t_s + q * 32; };
+        tmem_pipeline(q_end, s_col, [&](uint32_t(&v)[32], int q) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) mx4[k & 3] = fmaxf(mx4[k & 3], q * 32 + k < lim ? v[k] : -INFINITY);
-        }
+          for (int k = 0; k < 32; ++k)
+            mx4[k & 3] = fmaxf(mx4[k & 3], q * 32 + k < lim ? __uint_as_float(v[k]) : -INFINITY);
+        });
         const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         const float neg_mc = (mx == -INFINITY) ? 0.f : -mx * sl;
         // pass 2: P = 2^(s*c - m*c), packed fp16 over the scores already read
         float ls4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-        for (int q = 0; q < q_end; ++q) {
-          float v[32];
-          tmem_chunk(t_s + q * 32, v);
+        tmem_pipeline(q_end, s_col, [&](uint32_t(&v)[32], int q) {
           uint32_t w[16];
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
             const int c = q * 32 + k;
-            const float e0 = (c < lim) ? ex2_approx(fmaf(v[k], sl, neg_mc)) : 0.f;
-            const float e1 = (c + 1 < lim) ? ex2_approx(fmaf(v[k + 1], sl, neg_mc)) : 0.f;
+            const float e0 = (c < lim) ? ex2_approx(fmaf(__uint_as_float(v[k]), sl, neg_mc)) : 0.f;
+            const float e1 = (c + 1 < lim) ? ex2_approx(fmaf(__uint_as_float(v[k + 1]), sl, neg_mc)) : 0.f;
             ls4[(k >> 1) & 3] += e0 + e1;
             w[k / 2] = pack_half2(e0, e1);
           }
-          tmem_st16(t_s + q * 16, w);
-        }
+          tmem_st16(t_s + q * 16, w);  // P over scores this thread has already read
+        });
 #pragma unroll 1
         for (int q = q_end; q < 4; ++q) {
           uint32_t w[16];
@@ -553,10 +562,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       signal(&a_ready);
       // ---- u = gelu(h W1^T + b1) ----
       if (!wait_acc()) break;
-#pragma unroll 1
-      for (int q = 0; q < 4; ++q) {
+      tmem_pipeline(4, [&](int q) { return t_lane + kColAcc + q * 32; }, [&](uint32_t(&raw)[32], int q) {
         float a[32];
-        tmem_chunk(t_lane + kColAcc + q * 32, a);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) a[k] = __uint_as_float(raw[k]);
 #pragma unroll
         for (int u4 = 0; u4 < 4; ++u4) {
           const int c8 = q * 32 + u4 * 8;
@@ -573,7 +582,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* atom = sA + (u >> 3) * kAtomBytes;
           *reinterpret_cast<uint4*>(atom + r * 128 + swz_unit(r, u & 7, 8) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-      }
+      });
       signal(&a_ready);
       // ---- x += u W2^T + b2, padded rows zeroed; next LN1 or the final LN ----
       if (!wait_acc()) break;
