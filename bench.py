@@ -279,10 +279,18 @@ def run_sweep(args):
     (graph-replayed when a forward is short), warm-up, then the median of
     per-forward CUDA-event samples with an L2 flush between samples; one JSON
     line per case with the reference's best published T4 time beside it."""
+    import dataclasses
+
     import _tklib as tk
     import cuda_graphs
     import optimized
 
+    overrides = {}
+    for item in args.set:
+        key, _, value = item.partition("=")
+        overrides[key] = value == "True" if value in ("True", "False") else value
+    if overrides:
+        optimized.configure(**overrides)
     cases = sorted(APPENDIX) if args.sweep == "all" else [int(c) for c in args.sweep.split(",")]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -317,7 +325,8 @@ def run_sweep(args):
                 "ms": ms, "tokens_per_s": B * S * 1000.0 / ms, "samples": n,
                 "reference_t4_ms": t4_ms, "speedup_vs_reference_t4": t4_ms / ms,
                 "path": ("one-launch stack kernel" if model.settings.fused_small_stack
-                         and tk.lib().tk_stack_small_supported(d, H, ffn, S) else "per-layer kernels")}
+                         and tk.lib().tk_stack_small_supported(d, H, ffn, S) else "per-layer kernels"),
+                "settings": dataclasses.asdict(model.settings)}
         print(json.dumps(line), flush=True)
         del model, x
         torch.cuda.empty_cache()
@@ -422,6 +431,8 @@ def main() -> int:
     ap.add_argument("--e2e-chunks", type=int, default=4, help="batch slices of the streamed end-to-end forward")
     ap.add_argument("--sweep", default="", help="comma-separated appendix cases (or 'all'): one JSON line each, "
                                                 "timed like the harness (median of CUDA-event samples)")
+    ap.add_argument("--set", action="append", default=[], metavar="FIELD=VALUE",
+                    help="--sweep: override an OptimizerSettings field (e.g. fused_small_stack=False)")
     ap.add_argument("--strong", action="store_true",
                     help="one process drives --gpus local GPUs: the config's batch is split across them "
                          "(ShardedTransformer, NVLink scatter/gather) -- strong scaling")
