@@ -372,12 +372,12 @@ int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
     CUtensorMap mo = ma;  // unused by the staged residual epilogue
     p.reduce_add = (epilogue == TK_EPI_BIAS_RESID && resid == sum_out && ld_resid == ld_sum && row_len == nullptr);
     if (p.reduce_add) {
-      // in-place residual update: TMA reduce-add of 32 x 16 fp32 tiles into sum_out
+      // in-place residual update: TMA reduce-add of 32 x 32 fp32 tiles (128-byte swizzle) into sum_out
       cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
       cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_sum) * 4};
-      cuuint32_t box[2] = {16, 32};
+      cuuint32_t box[2] = {32, 32};
       if (int st = make_map(&mo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, sum_out, 2, dims, strides, box,
-                            CU_TENSOR_MAP_SWIZZLE_64B))
+                            CU_TENSOR_MAP_SWIZZLE_128B))
         return st;
     } else if (epilogue != TK_EPI_BIAS_RESID) {
       cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
