@@ -77,3 +77,29 @@ def test_layernorm_leaves_guard_bands_untouched(cuda_device):
     assert torch.all(buf[:pad] == -7.0) and torch.all(buf[-pad:] == -7.0)
     ref = layer_norm_reference(x.cpu(), w.cpu(), b.cpu(), 1e-5, torch.float32)
     torch.testing.assert_close(out.cpu(), ref, atol=1e-5, rtol=1e-5)
+
+
+# Plain norms with rows * d above the small-launch threshold and 512 < d <= 1024
+# (the forward's LN1 / LN2 / final norm) stream each row into shared memory with
+# one bulk copy; rows are ragged against the 8-warp blocks, and a strided input
+# keeps 16-byte row starts. d = 1020 with fp16 input (2040-byte rows) is not a
+# multiple of 16 bytes and takes the per-warp kernel.
+@pytest.mark.parametrize("d,x_dtype,out_dtype,pad_cols", [
+    (1024, torch.float32, torch.float16, 0),
+    (1024, torch.float32, torch.float32, 64),
+    (768, torch.float16, torch.float16, 0),
+    (1000, torch.float32, torch.float16, 8),
+    (1020, torch.float16, torch.float32, 0),
+])
+def test_layernorm_large_rows(cuda_device, d, x_dtype, out_dtype, pad_cols):
+    rows = 6007
+    full = seeded(rows, d + pad_cols, dtype=x_dtype, seed=d, scale=3.0)
+    x = full[:, :d]
+    w = seeded(d, seed=d + 1, scale=0.5) + 1.0
+    b = seeded(d, seed=d + 2, scale=0.5)
+    y = fused_kernels.ln_fwd(x, w, b, 1e-5, out_dtype)
+    ref = layer_norm_reference(x.float().cpu(), w.cpu(), b.cpu(), 1e-5, torch.float32)
+    if out_dtype == torch.float32:
+        torch.testing.assert_close(y.cpu(), ref, atol=1e-5, rtol=1e-5)
+    else:
+        torch.testing.assert_close(y.float().cpu(), ref, atol=2e-3, rtol=2e-2)
