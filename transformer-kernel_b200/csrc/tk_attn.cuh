@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
       const Item it = make_item(p, idx, q_tiles, q_pairs);
       const int tq = g == 0 ? it.tq0 : it.tq1;
-      const int n_g = it.last[g];
+      const int n_g = g == 0 ? it.last[0] : it.last[1];  // no runtime index: Item stays in registers
       const int q_idx = tq * kBM + r;
       float m = -INFINITY;  // running max, raw score units
       float l = 0.f;
