@@ -156,6 +156,24 @@ def test_gemm_pair_resid_in_place(cuda_device, M, N, K):
     torch.testing.assert_close(buf.cpu(), r + ref_linear(a, w, b), atol=1e-4, rtol=1e-4)
 
 
+def test_gemm_pair_resid_in_place_strided_guard_bands(cuda_device):
+    # The residual stream as a strided window of a guarded fp32 buffer: the
+    # TMA reduce-adds touch exactly the M x N window (the M tail is clipped,
+    # the columns past N and the guard bands keep their sentinel).
+    M, N, K, ld, pad = 9000, 1024, 512, 1024 + 32, 4096
+    a, w, b = operands(M, N, K, seed=61)
+    r = seeded(M, N, seed=62)
+    buf = torch.full((M * ld + 2 * pad,), -5.0, dtype=torch.float32, device="cuda")
+    win = buf[pad:pad + M * ld].view(M, ld)[:, :N]
+    win.copy_(r.cuda())
+    tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid", resid=win, sum_out=win)
+    torch.cuda.synchronize()
+    host = buf.cpu()
+    assert torch.all(host[:pad] == -5.0) and torch.all(host[-pad:] == -5.0)
+    assert torch.all(host[pad:pad + M * ld].view(M, ld)[:, N:] == -5.0)
+    torch.testing.assert_close(win.cpu(), r + ref_linear(a, w, b), atol=1e-4, rtol=1e-4)
+
+
 def test_gemm_pair_k_tail(cuda_device):
     # K = 320: the last 128-wide k stage of the pair kernel is half zero-filled
     M, N, K = 8192, 2048, 320
