@@ -59,9 +59,11 @@ constexpr int kColP = 256;  // P_g at kColP + 64 g (packed fp16 pairs)
 constexpr int kColO = 384;  // O_g at kColO + 64 g (fp32, HD <= 64 columns)
 constexpr float kLazyRescaleLog2 = 8.f;
 // Of every 8 consecutive score columns, this many take 2^x on the FMA pipe
-// (exp2_fma) instead of the SFU: the SFU (16 results/clk/SM) is the
-// softmax's bottleneck at head_dim 64, and the FMA pipe has room.
+// (exp2_fma_pair, two columns per f32x2 instruction) instead of the SFU: the
+// SFU (16 results/clk/SM) is the softmax's bottleneck at head_dim 64, and the
+// FMA pipe has room. Even, so that column pairs stay on one pipe.
 constexpr int kExpFmaPer8 = 2;
+static_assert(kExpFmaPer8 % 2 == 0, "FMA-pipe exponentials go in column pairs");
 
 // 2^x on the FMA/ALU pipes, for x <= 8 (scores minus the running max).
 // Cody-Waite style range reduction x = n + f with n = rint(x), |f| <= 1/2
@@ -78,6 +80,35 @@ __device__ __forceinline__ float exp2_fma(float x) {
   const float f = x - (t - kRound);
   const float q = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
   return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
+}
+
+// exp2_fma on a pair of values with f32x2 adds and FMAs (same operations, same results).
+__device__ __forceinline__ float2 exp2_fma_pair(float2 x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992811f, kC1 = 0.69326099f, kC2 = 0.24261054f, kC3 = 0.05517132f;
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = fadd2(x, splat2(kRound));
+  const float2 f = ffma2(fadd2(t, splat2(-kRound)), splat2(-1.f), x);
+  const float2 q = ffma2(ffma2(ffma2(splat2(kC3), f, splat2(kC2)), f, splat2(kC1)), f, splat2(kC0));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+// 2^x of score columns t and t + 1 (t even) in place: the pair goes to the
+// FMA pipe when its columns are among the last kExpFmaPer8 of their group of
+// eight, else each value to the SFU.
+__device__ __forceinline__ void exp2_cols(uint32_t& a, uint32_t& b, int t) {
+  const float2 x = make_float2(__uint_as_float(a), __uint_as_float(b));
+  float2 y;
+  if ((t & 7) >= 8 - kExpFmaPer8) {
+    y = exp2_fma_pair(x);
+  } else {
+    y.x = ex2_approx(x.x);
+    y.y = ex2_approx(x.y);
+  }
+  a = __float_as_uint(y.x);
+  b = __float_as_uint(y.y);
 }
 
 struct Params {
@@ -461,10 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              const float x = __uint_as_float(sv[c][t]);
-              sv[c][t] = __float_as_uint((t & 7) >= 8 - kExpFmaPer8 ? exp2_fma(x) : ex2_approx(x));
-            }
+            for (int t = 0; t < 32; t += 2) exp2_cols(sv[c][t], sv[c][t + 1], t);
           if (!full) {
 #pragma unroll
             for (int c = 0; c < 2; ++c)

@@ -307,10 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const float x = __uint_as_float(sv[c][t]);
-            sv[c][t] = __float_as_uint((t & 7) >= 8 - kExpFmaPer8 ? exp2_fma(x) : ex2_approx(x));
-          }
+          for (int t = 0; t < 32; t += 2) exp2_cols(sv[c][t], sv[c][t + 1], t);
         if (!full) {
 #pragma unroll
           for (int c = 0; c < 2; ++c)
