@@ -433,12 +433,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         lim = max(0, min(kBN, lim));
 
         // The score row is handled 64 columns at a time, so only half of it
-        // (plus its packed P) is ever live in registers: pass 1 takes the row
-        // max over both halves (the second half stays in registers), pass 2
-        // exponentiates the second half, then reloads and exponentiates the
-        // first; S_g is released to the MMA warp after that reload.
+        // (plus its packed P) is ever live in registers. Once every row of
+        // the warp has a finite running max m (from the second KV tile on),
+        // the first half is exponentiated against m while the row max is
+        // taken; if no row's max then grows by more than the lazy-rescale
+        // bound, m stays, the first half's P is kept and S_g is released as
+        // soon as the second half is in registers (one TMEM read of S).
+        // Otherwise (and on the first tile) the row max over both halves
+        // comes first: the second half is exponentiated, the first reloaded
+        // and exponentiated, and S_g released after that reload.
         const bool full = lim >= kBN;  // masking only on the causal diagonal / kv-bound tile
         uint32_t sv[2][32];
+        uint32_t pk[2][16];
+        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         auto row_max = [&](const int col0) {
           if (full) {
@@ -455,31 +462,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (col0 + c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
           }
         };
-        tmem_ld32(t_s, sv[0]);
-        tmem_ld32(t_s + 32, sv[1]);
-        tmem_ld_wait(sv[0]);
-        tmem_ld_wait(sv[1]);
-        row_max(0);
-        tmem_ld32(t_s + 64, sv[0]);
-        tmem_ld32(t_s + 96, sv[1]);
-        tmem_ld_wait(sv[0]);
-        tmem_ld_wait(sv[1]);
-        row_max(64);
-        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-        float m_use = m;
-        float alpha = 1.f;
-        if (mx > m) {
-          if (m == -INFINITY || (mx - m) * sl > kLazyRescaleLog2) {
-            alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - mx) * sl);
-            m_use = mx;
-          }
-        }
-        const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
-        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        auto load_half = [&](const int col0) {
+          tmem_ld32(t_s + col0, sv[0]);
+          tmem_ld32(t_s + col0 + 32, sv[1]);
+          tmem_ld_wait(sv[0]);
+          tmem_ld_wait(sv[1]);
+        };
         // P = 2^(s*c - m*c) for the 64 columns in sv starting at col0, in
-        // independent passes (exponents, then ex2, then sums and fp16
-        // packing), stored to P_g's TMEM columns.
-        auto exp_half = [&](const int col0) {
+        // independent passes (exponents, then 2^x, then sums and fp16
+        // packing into pk).
+        auto exp_half = [&](const int col0, const float neg_mc) {
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -500,7 +492,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int t = 0; t < 32; ++t)
                 if (col0 + c * 32 + t >= lim) sv[c][t] = 0u;
           }
-          uint32_t pk[2][16];
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -510,30 +501,74 @@ __global__ void __launch_bounds__(kThreads, 1)
               add2(rs[a], rs[a + 1], p0, p1);
               pk[c][t / 2] = pack_half2(p0, p1);
             }
+        };
+        auto store_half = [&](const int col0) {
 #pragma unroll
           for (int c = 0; c < 2; ++c) tmem_st16(t_p + col0 / 2 + c * 16, pk[c]);
         };
+        auto release_s = [&]() {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&s_free[g]);
+        };
+        const bool try_stale = __all_sync(0xffffffffu, m != -INFINITY);
+        const float neg_stale = try_stale ? -m * sl : 0.f;
+        load_half(0);
+        row_max(0);
+        if (try_stale) exp_half(0, neg_stale);
+        load_half(64);
+        row_max(64);
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+        float m_use = m;
+        float alpha = 1.f;
+        if (mx > m) {
+          if (m == -INFINITY || (mx - m) * sl > kLazyRescaleLog2) {
+            alpha = (m == -INFINITY) ? 0.f : ex2_approx((m - mx) * sl);
+            m_use = mx;
+          }
+        }
+        const bool keep = try_stale && !__any_sync(0xffffffffu, m_use != m);
         // PV_g of the previous tile reads P_g and writes O_g: it must be
         // complete before P_g is overwritten or O_g rescaled.
-        if (tiles > 0) {
-          if (!mbar_wait(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
-            report_error(kDevWaitTimeout, kid * 256 + kSitePv);
-            abort_flag = 1;
+        bool pv_ok = true;
+        auto wait_pv = [&]() {
+          if (tiles > 0) {
+            if (!mbar_wait(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+              report_error(kDevWaitTimeout, kid * 256 + kSitePv);
+              abort_flag = 1;
+              pv_ok = false;
+              return;
+            }
+            tc_fence_after();
+          }
+        };
+        if (keep) {
+          // S_g is fully consumed (first half as P in pk, second half in sv)
+          release_s();
+          wait_pv();
+          if (!pv_ok) {
             ok = false;
             break;
           }
-          tc_fence_after();
+          store_half(0);
+          exp_half(64, neg_stale);
+          store_half(64);
+        } else {
+#pragma unroll
+          for (int a = 0; a < 8; ++a) rs[a] = 0.f;
+          const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
+          wait_pv();
+          if (!pv_ok) {
+            ok = false;
+            break;
+          }
+          exp_half(64, neg_mc);
+          store_half(64);
+          load_half(0);
+          release_s();  // S_g is fully in registers: the MMA warp may compute the next tile's scores
+          exp_half(0, neg_mc);
+          store_half(0);
         }
-        exp_half(64);
-        tmem_ld32(t_s, sv[0]);
-        tmem_ld32(t_s + 32, sv[1]);
-        tmem_ld_wait(sv[0]);
-        tmem_ld_wait(sv[1]);
-        // S_g is fully in registers: the MMA warp may compute the next tile's scores
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&s_free[g]);
-        exp_half(0);
         const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
         const bool need = (j > 0) && (alpha != 1.f);
         if (__any_sync(0xffffffffu, need)) {
