@@ -1,7 +1,7 @@
 """Error bounds of the device-side approximations, restated on the CPU.
 
 The attention softmax takes a quarter of its exponentials on the FMA pipe
-(csrc/tk_attn.cuh exp2_fma / exp2_fma_pair: Cody-Waite reduction plus a cubic
+(csrc/tk_attn.cuh exp2_fma_pair: Cody-Waite reduction plus a cubic
 fitted for minimum relative error), and the FFN-in GEMM epilogue computes the
 erf GELU by Abramowitz & Stegun 7.1.28 (csrc/tk_gemm.cuh gelu_erf2). Both are
 restated here in float32 steps, with the constants parsed from the shipped

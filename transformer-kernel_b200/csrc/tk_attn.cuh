@@ -65,31 +65,21 @@ constexpr float kLazyRescaleLog2 = 8.f;
 constexpr int kExpFmaPer8 = 2;
 static_assert(kExpFmaPer8 % 2 == 0, "FMA-pipe exponentials go in column pairs");
 
-// 2^x on the FMA/ALU pipes, for x <= 8 (scores minus the running max).
-// Cody-Waite style range reduction x = n + f with n = rint(x), |f| <= 1/2
-// (adding 1.5 * 2^23 rounds x to an integer in the low mantissa bits), then
-// 2^f by a degree-3 polynomial fitted here for minimum maximum relative
-// error on [-1/2, 1/2] (7.5e-5, below the 2^-11 fp16 rounding that P gets),
-// and 2^n added into the exponent field. x is clamped at -126 so the
-// exponent cannot wrap; 2^-126 becomes 0 in the fp16 P.
-__device__ __forceinline__ float exp2_fma(float x) {
-  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
-  constexpr float kC0 = 0.99992811f, kC1 = 0.69326099f, kC2 = 0.24261054f, kC3 = 0.05517132f;
-  x = fmaxf(x, -126.f);
-  const float t = x + kRound;
-  const float f = x - (t - kRound);
-  const float q = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(t) << 23));
-}
-
-// exp2_fma on a pair of values with f32x2 adds and FMAs (same operations, same results).
+// 2^x on the FMA/ALU pipes for a pair of values x <= 8 (scores minus the
+// running max), two columns per f32x2 instruction. Cody-Waite style range
+// reduction x = n + f with n = rint(x), |f| <= 1/2 (adding 1.5 * 2^23 rounds
+// x to an integer in the low mantissa bits), then 2^f by a degree-3
+// polynomial fitted here for minimum maximum relative error on [-1/2, 1/2]
+// (7.5e-5, below the 2^-11 fp16 rounding that P gets), and 2^n added into
+// the exponent field. x is clamped at -126 so the exponent cannot wrap;
+// 2^-126 becomes 0 in the fp16 P.
 __device__ __forceinline__ float2 exp2_fma_pair(float2 x) {
   constexpr float kRound = 12582912.f;  // 1.5 * 2^23
   constexpr float kC0 = 0.99992811f, kC1 = 0.69326099f, kC2 = 0.24261054f, kC3 = 0.05517132f;
   x.x = fmaxf(x.x, -126.f);
   x.y = fmaxf(x.y, -126.f);
-  const float2 t = fadd2(x, splat2(kRound));
-  const float2 f = ffma2(fadd2(t, splat2(-kRound)), splat2(-1.f), x);
+  const float2 t = fadd2(x, splat2(kRound));                            // n + 1.5 * 2^23
+  const float2 f = ffma2(fadd2(t, splat2(-kRound)), splat2(-1.f), x);  // x - n
   const float2 q = ffma2(ffma2(ffma2(splat2(kC3), f, splat2(kC2)), f, splat2(kC1)), f, splat2(kC0));
   return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
                      __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
