@@ -40,3 +40,23 @@ def test_small_stack_declines_mixed_layernorm_eps():
     model.load_state_dict(init_params(cfg, seed=0), strict=True)
     model.layers[1].norm2.eps = 1e-6
     assert model._small_stack_pack(model._weights()) is None
+
+
+def test_state_dict_reload_rebuilds_the_weight_cache():
+    # load_state_dict copies into the existing parameters (same storage), so
+    # the derived fp16 copies must be rebuilt from the new values.
+    cfg = StackConfig(1, 8, 128, 4, 128, 2, True)
+    model = optimized.OptimizedTransformer(cfg)
+    model.load_state_dict(init_params(cfg, seed=0), strict=True)
+    first = model._weights()
+    model._small_stack_pack(first)
+    ptr = model.layers[0].attention.q_proj.weight.data_ptr()
+    fresh = init_params(cfg, seed=1)
+    model.load_state_dict(fresh, strict=True)
+    assert model.layers[0].attention.q_proj.weight.data_ptr() == ptr
+    again = model._weights()
+    assert again is not first
+    want = torch.cat([fresh[f"layers.1.attention.{n}_proj.weight"] for n in "qkv"], 0).half()
+    torch.testing.assert_close(again[1].qkv_w, want, atol=0, rtol=0)
+    w, _, _ = model._small_stack_pack(again)
+    torch.testing.assert_close(w[768:768 + 384], want, atol=0, rtol=0)

@@ -170,8 +170,21 @@ class OptimizedTransformer(nn.Module):
         self._weight_cache_key = None
         return result
 
+    def _load_from_state_dict(self, *args, **kwargs):
+        # A state-dict load copies into the existing parameters in place, so
+        # their storage (the cache key) does not change: drop the derived
+        # copies here. The reference relies on the load happening before the
+        # first forward (src/optimized.py:266-273); this also covers a reload
+        # after it.
+        self._weight_cache = None
+        self._weight_cache_key = None
+        return super()._load_from_state_dict(*args, **kwargs)
+
     @_outside_compile
     def _weights(self) -> List[_LayerWeights]:
+        """Per-layer fp16 GEMM weights (QKV concatenated) and fp32 bias /
+        LayerNorm vectors, built once per (device, dtype, storage) of the
+        parameters and dropped by ``_apply`` and by state-dict loads."""
         ref = self.layers[0].attention.q_proj.weight
         key = (ref.device, ref.dtype, ref.data_ptr())
         if self._weight_cache is not None and self._weight_cache_key == key:
