@@ -60,3 +60,14 @@ def test_state_dict_reload_rebuilds_the_weight_cache():
     torch.testing.assert_close(again[1].qkv_w, want, atol=0, rtol=0)
     w, _, _ = model._small_stack_pack(again)
     torch.testing.assert_close(w[768:768 + 384], want, atol=0, rtol=0)
+
+
+def test_state_dict_reload_drops_captured_graphs():
+    import cuda_graphs
+
+    cfg = StackConfig(1, 8, 128, 4, 128, 2, True)
+    model = cuda_graphs.GraphedTransformer(cfg)
+    model.load_state_dict(init_params(cfg, seed=0), strict=True)
+    model._graph_states[("shape",)] = cuda_graphs._GraphState()
+    model.load_state_dict(init_params(cfg, seed=1), strict=True)
+    assert model._graph_states == {}

@@ -49,6 +49,11 @@ class GraphedTransformer(OptimizedTransformer):
         self._graph_states = {}
         return result
 
+    def _load_from_state_dict(self, *args, **kwargs):
+        # the captured graphs read the weight copies that a load rebuilds
+        self._graph_states = {}
+        return super()._load_from_state_dict(*args, **kwargs)
+
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         lengths = self._prefix_lengths(valid_token_mask)
         key = (tuple(x.shape), x.dtype, x.device, None if lengths is None else tuple(lengths.tolist()))
