@@ -530,6 +530,13 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
     {
       std::lock_guard<std::mutex> lk(g_dev_mu);
       if (!info->attn_attr_set[slot]) {
+        if (threads == tk::attn::kThreads) {
+          // the in-kernel register split assumes this launch allocation
+          cudaFuncAttributes fa;
+          cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+          if (e != cudaSuccess) return e;
+          if (fa.numRegs != tk::attn::kLaunchRegs) return cudaErrorInvalidConfiguration;
+        }
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
         if (e != cudaSuccess) return e;
         info->attn_attr_set[slot] = true;

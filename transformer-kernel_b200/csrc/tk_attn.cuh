@@ -20,10 +20,12 @@
 // Persistent: one CTA per SM loops over work items (b, h, pair of 128-query
 // tiles), heaviest first; TMEM stays allocated, Q is double-buffered, the
 // K/V ring and all barrier phases run on across items, and the next item's
-// first S = QK^T overlaps the current item's epilogue. Warp roles:
-// warp 0 TMA, warp 1 TMEM owner + MMA issuer, warps 2..5 softmax group 0
-// (query tile 2p), warps 6..9 softmax group 1 (tile 2p+1); each softmax
-// thread owns one query row (its warp's TMEM lane quadrant). Both groups
+// first S = QK^T overlaps the current item's epilogue. Three warpgroups:
+// warp 0 TMA, warp 1 TMEM owner + MMA issuer (warps 2 and 3 have no role),
+// warps 4..7 softmax group 0 (query tile 2p), warps 8..11 softmax group 1
+// (tile 2p+1). setmaxnreg moves registers from the first warpgroup to the
+// softmax groups (224 per thread), so each softmax thread holds its query
+// row's whole 128-column score tile (its warp's TMEM lane quadrant). Both groups
 // share every K/V tile. TMEM (512 columns): S_g = Q_g K^T in columns
 // [128g, 128g+128) fp32, P_g = softmax numerators as packed fp16 pairs in
 // [256+64g, 320+64g), O_g in [384+64g, 384+64g+HD).
@@ -52,7 +54,20 @@ namespace attn {
 
 constexpr int kBM = 128;  // queries per tile (two tiles per CTA)
 constexpr int kBN = 128;  // keys per KV tile
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// Register split (setmaxnreg): the kernel is built for kLaunchRegs registers
+// per thread (the 384-thread cap of 65,536 / 384, rounded down to 8); warpgroup
+// 0 (TMA, MMA, two idle warps) drops to kProducerRegs and the two softmax
+// warpgroups take what it frees. The split uses exactly the launch allocation
+// (an inc above it would wait forever), and each sub-partition holds one
+// warpgroup-0 warp and two softmax warps: 56 * 32 + 2 * 224 * 32 = 16,128 of
+// its 16,384 registers. The host refuses to launch if the built register
+// count is not kLaunchRegs.
+constexpr int kLaunchRegs = 168;
+constexpr int kProducerRegs = 56;
+constexpr int kSoftmaxRegs = 224;
+static_assert(4 * 32 * kProducerRegs + 8 * 32 * kSoftmaxRegs == kThreads * kLaunchRegs, "register split");
+static_assert(kProducerRegs * 32 + 2 * kSoftmaxRegs * 32 <= 16384, "sub-partition register file");
 constexpr int kStages = 4;
 constexpr int kTmemCols = 512;
 constexpr int kColP = 256;  // P_g at kColP + 64 g (packed fp16 pairs)
@@ -226,172 +241,178 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = tmem_base_sh;
   grid_dep_wait();  // the previous kernel's outputs are complete and visible
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      prefetch_tensormap(&map_q);
-      prefetch_tensormap(&map_k);
-      prefetch_tensormap(&map_v);
-      int kv_count = 0;  // KV tiles loaded so far (ring position)
-      int qn = 0;        // items with work loaded so far (Q buffer set = qn & 1)
-      bool ok = true;
-      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
-        const Item it = make_item(p, idx, q_tiles, q_pairs);
-        if (it.n_kv == 0) continue;
-        const int qs = qn & 1;
-        const uint32_t q_phase = (qn >> 1) & 1;
-        ++qn;
-        if (!mbar_wait(&q_empty[qs], q_phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
-          report_error(kDevWaitTimeout, kid * 256 + kSiteQEmpty);
-          abort_flag = 1;
-          ok = false;
-          break;
-        }
-        uint8_t* q_dst = sQ + qs * 2 * C::TILE_BYTES;
-        mbar_arrive_expect_tx(&q_full[qs], C::TILE_BYTES * (it.has1 ? 2 : 1));
-        load_tile(q_dst, &map_q, &q_full[qs], p, it.tq0 * kBM, it.h, it.b);
-        if (it.has1) load_tile(q_dst + C::TILE_BYTES, &map_q, &q_full[qs], p, it.tq1 * kBM, it.h, it.b);
-        for (int j = 0; j < it.n_kv; ++j, ++kv_count) {
-          const int s = kv_count % kStages;
-          const uint32_t ph = (kv_count / kStages) & 1;
-          if (!mbar_wait(&kv_empty[s], ph ^ 1u, &abort_flag, p.wait_limit_ns)) {
-            report_error(kDevWaitTimeout, kid * 256 + kSiteEmpty);
+  // Register split: every warp of a warpgroup executes the same setmaxnreg,
+  // which dominates that warpgroup's role code.
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+    if (warp == 0) {
+      // ---------------- TMA producer ----------------
+      if (lane == 0) {
+        prefetch_tensormap(&map_q);
+        prefetch_tensormap(&map_k);
+        prefetch_tensormap(&map_v);
+        int kv_count = 0;  // KV tiles loaded so far (ring position)
+        int qn = 0;        // items with work loaded so far (Q buffer set = qn & 1)
+        bool ok = true;
+        for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+          const Item it = make_item(p, idx, q_tiles, q_pairs);
+          if (it.n_kv == 0) continue;
+          const int qs = qn & 1;
+          const uint32_t q_phase = (qn >> 1) & 1;
+          ++qn;
+          if (!mbar_wait(&q_empty[qs], q_phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSiteQEmpty);
             abort_flag = 1;
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&kv_full[s], 2 * C::TILE_BYTES);
-          load_tile(sK + s * C::TILE_BYTES, &map_k, &kv_full[s], p, j * kBN, it.h, it.b);
-          load_tile(sV + s * C::TILE_BYTES, &map_v, &kv_full[s], p, j * kBN, it.h, it.b);
+          uint8_t* q_dst = sQ + qs * 2 * C::TILE_BYTES;
+          mbar_arrive_expect_tx(&q_full[qs], C::TILE_BYTES * (it.has1 ? 2 : 1));
+          load_tile(q_dst, &map_q, &q_full[qs], p, it.tq0 * kBM, it.h, it.b);
+          if (it.has1) load_tile(q_dst + C::TILE_BYTES, &map_q, &q_full[qs], p, it.tq1 * kBM, it.h, it.b);
+          for (int j = 0; j < it.n_kv; ++j, ++kv_count) {
+            const int s = kv_count % kStages;
+            const uint32_t ph = (kv_count / kStages) & 1;
+            if (!mbar_wait(&kv_empty[s], ph ^ 1u, &abort_flag, p.wait_limit_ns)) {
+              report_error(kDevWaitTimeout, kid * 256 + kSiteEmpty);
+              abort_flag = 1;
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&kv_full[s], 2 * C::TILE_BYTES);
+            load_tile(sK + s * C::TILE_BYTES, &map_k, &kv_full[s], p, j * kBN, it.h, it.b);
+            load_tile(sV + s * C::TILE_BYTES, &map_v, &kv_full[s], p, j * kBN, it.h, it.b);
+          }
+        }
+        // all of this CTA's loads are issued: the next kernel may be scheduled
+        grid_dep_launch();
+        if (!ok) {
+          // let copies already in flight land before the CTA can exit
+          for (int t = max(0, kv_count - kStages); t < kv_count; ++t)
+            mbar_wait(&kv_full[t % kStages], (t / kStages) & 1, nullptr, kDrainLimitNs);
         }
       }
-      // all of this CTA's loads are issued: the next kernel may be scheduled
-      grid_dep_launch();
-      if (!ok) {
-        // let copies already in flight land before the CTA can exit
-        for (int t = max(0, kv_count - kStages); t < kv_count; ++t)
-          mbar_wait(&kv_full[t % kStages], (t / kStages) & 1, nullptr, kDrainLimitNs);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
-      constexpr uint32_t idesc_o = idesc_f16_f32(kBM, HD, false, true);
-      // Per-group counters live in named scalars and every per-group step is
-      // expanded for g = 0 and g = 1 separately, so nothing on this
-      // single-thread critical path is indexed dynamically (local memory).
-      struct Group {
-        int tiles = 0;     // tiles handed over by the softmax (p_full phases)
-        int o_uses = 0;    // items in which O_g was accumulated (o_full / o_free phases)
-        int s_issued = 0;  // S_g MMAs issued (s_free phases)
-      };
-      Group grp0, grp1;
-      int kv_count = 0;  // KV tiles consumed so far (ring position)
-      int qn = 0;        // items with work consumed so far (Q buffer set = qn & 1)
-      bool ok = true;
-      auto fail = [&](unsigned site) {
-        report_error(kDevWaitTimeout, kid * 256 + site);
-        ok = false;
-      };
-      for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
-        const Item it = make_item(p, idx, q_tiles, q_pairs);
-        if (it.n_kv == 0) continue;
-        const int last0 = it.last[0], last1 = it.last[1];
-        const int qs = qn & 1;
-        const uint32_t q_phase = (qn >> 1) & 1;
-        ++qn;
-        if (!mbar_wait(&q_full[qs], q_phase, &abort_flag, p.wait_limit_ns)) {
-          fail(kSiteQ);
-          break;
+      __syncwarp();
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0) {
+        constexpr uint32_t idesc_s = idesc_f16_f32(kBM, kBN, false, false);
+        constexpr uint32_t idesc_o = idesc_f16_f32(kBM, HD, false, true);
+        // Per-group counters live in named scalars and every per-group step is
+        // expanded for g = 0 and g = 1 separately, so nothing on this
+        // single-thread critical path is indexed dynamically (local memory).
+        struct Group {
+          int tiles = 0;     // tiles handed over by the softmax (p_full phases)
+          int o_uses = 0;    // items in which O_g was accumulated (o_full / o_free phases)
+          int s_issued = 0;  // S_g MMAs issued (s_free phases)
+        };
+        Group grp0, grp1;
+        int kv_count = 0;  // KV tiles consumed so far (ring position)
+        int qn = 0;        // items with work consumed so far (Q buffer set = qn & 1)
+        bool ok = true;
+        auto fail = [&](unsigned site) {
+          report_error(kDevWaitTimeout, kid * 256 + site);
+          ok = false;
+        };
+        for (int idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+          const Item it = make_item(p, idx, q_tiles, q_pairs);
+          if (it.n_kv == 0) continue;
+          const int last0 = it.last[0], last1 = it.last[1];
+          const int qs = qn & 1;
+          const uint32_t q_phase = (qn >> 1) & 1;
+          ++qn;
+          if (!mbar_wait(&q_full[qs], q_phase, &abort_flag, p.wait_limit_ns)) {
+            fail(kSiteQ);
+            break;
+          }
+          const int kv_base = kv_count;
+          int kv_ready = -1;
+          auto wait_kv = [&](int j) -> bool {
+            if (j <= kv_ready) return true;
+            const int t = kv_base + j;
+            if (!mbar_wait(&kv_full[t % kStages], (t / kStages) & 1, &abort_flag, p.wait_limit_ns)) {
+              fail(kSiteKV);
+              return false;
+            }
+            kv_ready = j;
+            return true;
+          };
+          // S_g(j) overwrites S_g: the softmax must have pulled the previous
+          // scores of group g into registers (s_free) first.
+          auto issue_s = [&](Group& gs, const int g, int j) {
+            if (!ok) return;
+            if (!wait_kv(j)) return;
+            if (gs.s_issued > 0 && !mbar_wait(&s_free[g], (gs.s_issued - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+              fail(kSiteSFree);
+              return;
+            }
+            ++gs.s_issued;
+            tc_fence_after();
+            const uint32_t q_addr = smem_u32(sQ + (qs * 2 + g) * C::TILE_BYTES);
+            const uint32_t k_addr = smem_u32(sK + ((kv_base + j) % kStages) * C::TILE_BYTES);
+  #pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
+              const uint64_t dq = smem_desc(q_addr + kk * 32, 16, C::SBO, C::LAYOUT);
+              const uint64_t dk = smem_desc(k_addr + kk * 32, 16, C::SBO, C::LAYOUT);
+              mma_f16_ss(tmem_base + g * kBN, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&s_full[g]);
+          };
+          // O_g += P_g(j) V_j once group g has written P_g(j) (p_full).
+          auto issue_pv = [&](Group& gs, const int g, int j, int last_g, bool last_reader) {
+            if (!ok) return;
+            if (!mbar_wait(&p_full[g], gs.tiles & 1, &abort_flag, p.wait_limit_ns)) {
+              fail(kSiteP);
+              return;
+            }
+            ++gs.tiles;
+            if (j == 0 && gs.o_uses > 0 &&
+                !mbar_wait(&o_free[g], (gs.o_uses - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+              // the previous item's epilogue of group g must be done reading O_g
+              fail(kSiteOFree);
+              return;
+            }
+            tc_fence_after();
+            const uint32_t v_addr = smem_u32(sV + ((kv_base + j) % kStages) * C::TILE_BYTES);
+  #pragma unroll
+            for (int ks = 0; ks < kBN / 16; ++ks) {
+              const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
+              mma_f16_ts(tmem_base + kColO + g * 64, tmem_base + kColP + g * 64 + ks * 8, dv, idesc_o,
+                         (j > 0 || ks > 0) ? 1u : 0u);
+            }
+            mma_commit(&pv_done[g]);  // P_g and O_g free for the softmax of tile j+1
+            if (last_reader) mma_commit(&kv_empty[(kv_base + j) % kStages]);  // K_j / V_j released
+            if (j + 1 == last_g) {
+              mma_commit(&o_full[g]);
+              ++gs.o_uses;
+            }
+          };
+          if (last0 > 0) issue_s(grp0, 0, 0);
+          if (last1 > 0) issue_s(grp1, 1, 0);
+          for (int j = 0; j < it.n_kv && ok; ++j) {
+            // S_g(j+1) as soon as group g has pulled S_g(j) into registers, so the
+            // next scores are computed during tile j's exponentials.
+            if (j + 1 < last0) issue_s(grp0, 0, j + 1);
+            if (j + 1 < last1) issue_s(grp1, 1, j + 1);
+            // the last reader of K_j / V_j (group 1 when it attends tile j) releases the stage
+            if (j < last0) issue_pv(grp0, 0, j, last0, j >= last1);
+            if (j < last1) issue_pv(grp1, 1, j, last1, true);
+          }
+          if (!ok) break;
+          mma_commit(&q_empty[qs]);  // every S of this item read its Q set
+          kv_count += it.n_kv;
         }
-        const int kv_base = kv_count;
-        int kv_ready = -1;
-        auto wait_kv = [&](int j) -> bool {
-          if (j <= kv_ready) return true;
-          const int t = kv_base + j;
-          if (!mbar_wait(&kv_full[t % kStages], (t / kStages) & 1, &abort_flag, p.wait_limit_ns)) {
-            fail(kSiteKV);
-            return false;
-          }
-          kv_ready = j;
-          return true;
-        };
-        // S_g(j) overwrites S_g: the softmax must have pulled the previous
-        // scores of group g into registers (s_free) first.
-        auto issue_s = [&](Group& gs, const int g, int j) {
-          if (!ok) return;
-          if (!wait_kv(j)) return;
-          if (gs.s_issued > 0 && !mbar_wait(&s_free[g], (gs.s_issued - 1) & 1, &abort_flag, p.wait_limit_ns)) {
-            fail(kSiteSFree);
-            return;
-          }
-          ++gs.s_issued;
-          tc_fence_after();
-          const uint32_t q_addr = smem_u32(sQ + (qs * 2 + g) * C::TILE_BYTES);
-          const uint32_t k_addr = smem_u32(sK + ((kv_base + j) % kStages) * C::TILE_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t dq = smem_desc(q_addr + kk * 32, 16, C::SBO, C::LAYOUT);
-            const uint64_t dk = smem_desc(k_addr + kk * 32, 16, C::SBO, C::LAYOUT);
-            mma_f16_ss(tmem_base + g * kBN, dq, dk, idesc_s, kk > 0 ? 1u : 0u);
-          }
-          mma_commit(&s_full[g]);
-        };
-        // O_g += P_g(j) V_j once group g has written P_g(j) (p_full).
-        auto issue_pv = [&](Group& gs, const int g, int j, int last_g, bool last_reader) {
-          if (!ok) return;
-          if (!mbar_wait(&p_full[g], gs.tiles & 1, &abort_flag, p.wait_limit_ns)) {
-            fail(kSiteP);
-            return;
-          }
-          ++gs.tiles;
-          if (j == 0 && gs.o_uses > 0 &&
-              !mbar_wait(&o_free[g], (gs.o_uses - 1) & 1, &abort_flag, p.wait_limit_ns)) {
-            // the previous item's epilogue of group g must be done reading O_g
-            fail(kSiteOFree);
-            return;
-          }
-          tc_fence_after();
-          const uint32_t v_addr = smem_u32(sV + ((kv_base + j) % kStages) * C::TILE_BYTES);
-#pragma unroll
-          for (int ks = 0; ks < kBN / 16; ++ks) {
-            const uint64_t dv = smem_desc(v_addr + ks * 16 * C::ROW_BYTES, C::TILE_BYTES, C::SBO, C::LAYOUT);
-            mma_f16_ts(tmem_base + kColO + g * 64, tmem_base + kColP + g * 64 + ks * 8, dv, idesc_o,
-                       (j > 0 || ks > 0) ? 1u : 0u);
-          }
-          mma_commit(&pv_done[g]);  // P_g and O_g free for the softmax of tile j+1
-          if (last_reader) mma_commit(&kv_empty[(kv_base + j) % kStages]);  // K_j / V_j released
-          if (j + 1 == last_g) {
-            mma_commit(&o_full[g]);
-            ++gs.o_uses;
-          }
-        };
-        if (last0 > 0) issue_s(grp0, 0, 0);
-        if (last1 > 0) issue_s(grp1, 1, 0);
-        for (int j = 0; j < it.n_kv && ok; ++j) {
-          // S_g(j+1) as soon as group g has pulled S_g(j) into registers, so the
-          // next scores are computed during tile j's exponentials.
-          if (j + 1 < last0) issue_s(grp0, 0, j + 1);
-          if (j + 1 < last1) issue_s(grp1, 1, j + 1);
-          // the last reader of K_j / V_j (group 1 when it attends tile j) releases the stage
-          if (j < last0) issue_pv(grp0, 0, j, last0, j >= last1);
-          if (j < last1) issue_pv(grp1, 1, j, last1, true);
-        }
-        if (!ok) break;
-        mma_commit(&q_empty[qs]);  // every S of this item read its Q set
-        kv_count += it.n_kv;
+        // everything issued is complete before TMEM can be released
+        mma_commit(&drain_bar);
+        mbar_wait(&drain_bar, 0, nullptr, ok ? p.wait_limit_ns : kDrainLimitNs);
+        if (!ok) abort_flag = 1;
       }
-      // everything issued is complete before TMEM can be released
-      mma_commit(&drain_bar);
-      mbar_wait(&drain_bar, 0, nullptr, ok ? p.wait_limit_ns : kDrainLimitNs);
-      if (!ok) abort_flag = 1;
-    }
-    __syncwarp();
+      __syncwarp();
+    }  // warps 2 and 3: no role
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ---------------- softmax, group g, one query row per thread ----------------
-    const int g = (warp - 2) >> 2;
+    const int g = (warp - 4) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + static_cast<int>(lane);
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
@@ -422,92 +443,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.causal) lim = min(lim, q_idx - k0 + 1);
         lim = max(0, min(kBN, lim));
 
-        // The score row is handled 64 columns at a time, so only half of it
-        // (plus its packed P) is ever live in registers. Once every row of
-        // the warp has a finite running max m (from the second KV tile on),
-        // the first half is exponentiated against m while the row max is
-        // taken; if no row's max then grows by more than the lazy-rescale
-        // bound, m stays, the first half's P is kept and S_g is released as
-        // soon as the second half is in registers (one TMEM read of S).
-        // Otherwise (and on the first tile) the row max over both halves
-        // comes first: the second half is exponentiated, the first reloaded
-        // and exponentiated, and S_g released after that reload.
+        // The whole 128-column score row is pulled into registers with one
+        // TMEM read and S_g is released to the MMA warp at once, so S_g(j+1)
+        // is computed during this tile's exponentials. Then: row max, lazy
+        // rescale decision, exponentials, fp16 packing with the row sums,
+        // and P_g stored once PV_g(j-1) has read the previous P.
         const bool full = lim >= kBN;  // masking only on the causal diagonal / kv-bound tile
-        uint32_t sv[2][32];
-        uint32_t pk[2][16];
-        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t sv[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, sv[c]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld_wait(sv[c]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[g]);
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        auto row_max = [&](const int col0) {
-          if (full) {
+        if (full) {
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-              for (int t = 0; t < 32; t += 2)
-                mx4[(t >> 1) & 3] = max3(mx4[(t >> 1) & 3], __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]));
-          } else {
+            for (int t = 0; t < 32; t += 2)
+              mx4[(t >> 1) & 3] = max3(mx4[(t >> 1) & 3], __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]));
+        } else {
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-              for (int t = 0; t < 32; ++t)
-                if (col0 + c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
-          }
-        };
-        auto load_half = [&](const int col0) {
-          tmem_ld32(t_s + col0, sv[0]);
-          tmem_ld32(t_s + col0 + 32, sv[1]);
-          tmem_ld_wait(sv[0]);
-          tmem_ld_wait(sv[1]);
-        };
-        // P = 2^(s*c - m*c) for the 64 columns in sv starting at col0, in
-        // independent passes (exponents, then 2^x, then sums and fp16
-        // packing into pk).
-        auto exp_half = [&](const int col0, const float neg_mc) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int t = 0; t < 32; t += 2) {
-              float x0, x1;
-              fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
-              sv[c][t] = __float_as_uint(x0);
-              sv[c][t + 1] = __float_as_uint(x1);
-            }
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int t = 0; t < 32; t += 2) exp2_cols(sv[c][t], sv[c][t + 1], t);
-          if (!full) {
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-              for (int t = 0; t < 32; ++t)
-                if (col0 + c * 32 + t >= lim) sv[c][t] = 0u;
-          }
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int t = 0; t < 32; t += 2) {
-              const float p0 = __uint_as_float(sv[c][t]), p1 = __uint_as_float(sv[c][t + 1]);
-              const int a = ((t >> 1) & 3) * 2;
-              add2(rs[a], rs[a + 1], p0, p1);
-              pk[c][t / 2] = pack_half2(p0, p1);
-            }
-        };
-        auto store_half = [&](const int col0) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) tmem_st16(t_p + col0 / 2 + c * 16, pk[c]);
-        };
-        auto release_s = [&]() {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&s_free[g]);
-        };
-        const bool try_stale = __all_sync(0xffffffffu, m != -INFINITY);
-        const float neg_stale = try_stale ? -m * sl : 0.f;
-        load_half(0);
-        row_max(0);
-        if (try_stale) exp_half(0, neg_stale);
-        load_half(64);
-        row_max(64);
+            for (int t = 0; t < 32; ++t)
+              if (c * 32 + t < lim) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(sv[c][t]));
+        }
         const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         float m_use = m;
         float alpha = 1.f;
@@ -517,48 +480,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_use = mx;
           }
         }
-        const bool keep = try_stale && !__any_sync(0xffffffffu, m_use != m);
+        const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            float x0, x1;
+            fma2(x0, x1, __uint_as_float(sv[c][t]), __uint_as_float(sv[c][t + 1]), sl, neg_mc);
+            sv[c][t] = __float_as_uint(x0);
+            sv[c][t + 1] = __float_as_uint(x1);
+          }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) exp2_cols(sv[c][t], sv[c][t + 1], t);
+        if (!full) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int t = 0; t < 32; ++t)
+              if (c * 32 + t >= lim) sv[c][t] = 0u;
+        }
+        float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[4][16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int t = 0; t < 32; t += 2) {
+            const float p0 = __uint_as_float(sv[c][t]), p1 = __uint_as_float(sv[c][t + 1]);
+            const int a = ((t >> 1) & 3) * 2;
+            add2(rs[a], rs[a + 1], p0, p1);
+            pk[c][t / 2] = pack_half2(p0, p1);
+          }
         // PV_g of the previous tile reads P_g and writes O_g: it must be
         // complete before P_g is overwritten or O_g rescaled.
-        bool pv_ok = true;
-        auto wait_pv = [&]() {
-          if (tiles > 0) {
-            if (!mbar_wait(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
-              report_error(kDevWaitTimeout, kid * 256 + kSitePv);
-              abort_flag = 1;
-              pv_ok = false;
-              return;
-            }
-            tc_fence_after();
-          }
-        };
-        if (keep) {
-          // S_g is fully consumed (first half as P in pk, second half in sv)
-          release_s();
-          wait_pv();
-          if (!pv_ok) {
+        if (tiles > 0) {
+          if (!mbar_wait(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+            report_error(kDevWaitTimeout, kid * 256 + kSitePv);
+            abort_flag = 1;
             ok = false;
             break;
           }
-          store_half(0);
-          exp_half(64, neg_stale);
-          store_half(64);
-        } else {
-#pragma unroll
-          for (int a = 0; a < 8; ++a) rs[a] = 0.f;
-          const float neg_mc = (m_use == -INFINITY) ? 0.f : -m_use * sl;
-          wait_pv();
-          if (!pv_ok) {
-            ok = false;
-            break;
-          }
-          exp_half(64, neg_mc);
-          store_half(64);
-          load_half(0);
-          release_s();  // S_g is fully in registers: the MMA warp may compute the next tile's scores
-          exp_half(0, neg_mc);
-          store_half(0);
+          tc_fence_after();
         }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_st16(t_p + c * 16, pk[c]);
         const float row_sum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
         const bool need = (j > 0) && (alpha != 1.f);
         if (__any_sync(0xffffffffu, need)) {
@@ -626,7 +592,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
