@@ -526,16 +526,22 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
   const int64_t items = B * H * ((q_tiles + 1) / 2);
   const unsigned grid = static_cast<unsigned>(items < info->sms ? items : info->sms);
   const bool small = static_cast<double>(B) * H * S * S * hd <= kSmallAttnWork;
+  int built_regs = 0;  // set when a kernel's register count does not match its register split
   auto run = [&](auto kern, int slot, int smem_bytes, unsigned grid_x, unsigned threads) -> cudaError_t {
     {
       std::lock_guard<std::mutex> lk(g_dev_mu);
       if (!info->attn_attr_set[slot]) {
         if (threads == tk::attn::kThreads) {
-          // the in-kernel register split assumes this launch allocation
+          // The in-kernel setmaxnreg split hands out exactly threads x
+          // kLaunchRegs registers; with any other launch allocation the
+          // softmax warpgroups' increase could never be granted.
           cudaFuncAttributes fa;
           cudaError_t e = cudaFuncGetAttributes(&fa, kern);
           if (e != cudaSuccess) return e;
-          if (fa.numRegs != tk::attn::kLaunchRegs) return cudaErrorInvalidConfiguration;
+          if (fa.numRegs != tk::attn::kLaunchRegs) {
+            built_regs = fa.numRegs;
+            return cudaErrorInvalidConfiguration;
+          }
         }
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
         if (e != cudaSuccess) return e;
@@ -558,6 +564,9 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
     e = run(tk::attn::attn_fwd_kernel<32>, 1, tk::attn::Cfg<32>::SMEM_BYTES, grid, kT);
   else
     e = run(tk::attn::attn_fwd_kernel<16>, 0, tk::attn::Cfg<16>::SMEM_BYTES, grid, kT);
+  if (built_regs != 0)
+    return fail(TK_ERR_LAUNCH, "tk_attn_fwd: kernel built with %d registers per thread; its register split needs %d",
+                built_regs, tk::attn::kLaunchRegs);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tk_attn_fwd launch");
   return TK_OK;
