@@ -71,3 +71,28 @@ def test_state_dict_reload_drops_captured_graphs():
     model._graph_states[("shape",)] = cuda_graphs._GraphState()
     model.load_state_dict(init_params(cfg, seed=1), strict=True)
     assert model._graph_states == {}
+
+
+def test_forward_paths_are_opaque_to_torch_compile():
+    # the harness may torch.compile the drop-in (--compile-user); every entry
+    # point runs eagerly inside a compiled caller
+    import cuda_graphs
+    import sharded
+
+    for fn in (optimized.OptimizedTransformer.forward, optimized.OptimizedTransformer.forward_from_host,
+               optimized.OptimizedTransformer._weights, optimized.OptimizedTransformer._prefix_lengths,
+               cuda_graphs.GraphedTransformer.forward, sharded.ShardedTransformer.forward):
+        assert getattr(fn, "_torchdynamo_disable", False), fn
+
+
+def test_compiled_model_runs_the_eager_forward():
+    # torch.compile around the drop-in reaches the library's own argument
+    # checks (a CPU input is refused) instead of tracing into the launches
+    import pytest
+    import _tklib as tk
+
+    cfg = StackConfig(1, 8, 128, 4, 128, 1, True)
+    model = optimized.OptimizedTransformer(cfg)
+    compiled = torch.compile(model, backend="eager")
+    with pytest.raises(tk.TKError):
+        compiled(torch.randn(1, 8, 128))

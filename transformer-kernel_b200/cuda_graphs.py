@@ -19,7 +19,7 @@ from typing import Dict, Optional, Tuple
 
 import torch
 
-from optimized import OptimizedTransformer
+from optimized import OptimizedTransformer, _outside_compile
 
 __all__ = ["GraphedTransformer", "WARMUP_BEFORE_CAPTURE"]
 
@@ -54,6 +54,7 @@ class GraphedTransformer(OptimizedTransformer):
         self._graph_states = {}
         return super()._load_from_state_dict(*args, **kwargs)
 
+    @_outside_compile
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         lengths = self._prefix_lengths(valid_token_mask)
         key = (tuple(x.shape), x.dtype, x.device, None if lengths is None else tuple(lengths.tolist()))

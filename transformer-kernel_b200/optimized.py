@@ -252,6 +252,12 @@ class OptimizedTransformer(nn.Module):
         return result
 
     # -- forward --------------------------------------------------------------
+    # The forward is opaque to torch.compile (the harness's --compile-user
+    # wraps the model, src/torch_transformer_benchmark.py:586-591,703): it is
+    # a sequence of library launches on raw pointers with nothing for dynamo
+    # to trace, and its cached buffers must stay ordinary allocations
+    # (src/optimized.py:64-77 keeps its cache builders out for that reason).
+    @_outside_compile
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not x.is_cuda:
             raise tk.TKError("forward", -1, "OptimizedTransformer runs on the B200 kernels only; x must be a CUDA tensor")
@@ -411,6 +417,7 @@ class OptimizedTransformer(nn.Module):
         return out.view(B, S, d)
 
     # -- host-streamed forward --------------------------------------------------
+    @_outside_compile
     def forward_from_host(
         self,
         x_host: torch.Tensor,

@@ -91,6 +91,7 @@ class ShardedTransformer(torch.nn.Module):
             self._bufs = {key: bufs}
         return bufs
 
+    @optimized._outside_compile
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         home = self.devices[0]
         if x.device != home:
