@@ -16,6 +16,7 @@ from __future__ import annotations
 import argparse
 import os
 import pathlib
+import re
 import shutil
 import subprocess
 import sys
@@ -43,6 +44,40 @@ def nvcc() -> str:
     return cand
 
 
+def kernel_resources(ptxas_log: str) -> dict:
+    """{mangled kernel name: (registers, spill store bytes)} from ptxas -v output."""
+    out, name, spill = {}, None, 0
+    for line in ptxas_log.splitlines():
+        m = re.search(r"Compiling entry function '([^']+)'", line)
+        if m:
+            name, spill = m.group(1), 0
+            continue
+        m = re.search(r"(\d+) bytes spill stores", line)
+        if m and name:
+            spill = int(m.group(1))
+            continue
+        m = re.search(r"Used (\d+) registers", line)
+        if m and name:
+            out[name] = (int(m.group(1)), spill)
+            name = None
+    return out
+
+
+def check_register_split(ptxas_log: str) -> None:
+    """The persistent attention kernel splits its launch allocation with
+    setmaxnreg (csrc/tk_attn.cuh kLaunchRegs): it must build with exactly
+    that many registers per thread and without spills."""
+    text = (HERE / "csrc" / "tk_attn.cuh").read_text()
+    want = int(re.search(r"constexpr int kLaunchRegs = (\d+);", text).group(1))
+    found = {k: v for k, v in kernel_resources(ptxas_log).items() if "attn15attn_fwd_kernel" in k}
+    if not found:
+        raise RuntimeError("ptxas output lists no attn_fwd_kernel")
+    bad = {k: v for k, v in found.items() if v != (want, 0)}
+    if bad:
+        raise RuntimeError(f"attn_fwd_kernel needs {want} registers and no spills for its register split; "
+                           f"ptxas gave (registers, spill bytes) {sorted(bad.values())}")
+
+
 def up_to_date() -> bool:
     if not LIB.exists():
         return False
@@ -61,6 +96,7 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
         raise RuntimeError(f"nvcc failed ({res.returncode})")
     if verbose:
         sys.stderr.write(res.stderr)
+    check_register_split(res.stdout + res.stderr)
     os.replace(tmp, LIB)
     return LIB
 
