@@ -48,7 +48,9 @@ typedef enum tk_epilogue {
 
 /* Row LayerNorm, optionally fused with a residual add.
  *   y == NULL : out = LN(x)                      -- replaces ln_fwd
- *               (src/fused_kernels.py:164-193)
+ *               (src/fused_kernels.py:164-193); with sum_out non-NULL the
+ *               input rows are also copied to sum_out (x's dtype), so a
+ *               forward can start its residual stream in its own buffer
  *   y != NULL : s = x + y (fp32 math, stored in x's dtype when sum_out is
  *               non-NULL); out = LN(s)          -- replaces add_ln_fwd
  *               (src/fused_kernels.py:196-238)

@@ -138,15 +138,45 @@ def test_cuda_graph_replay_matches_eager(cuda_device):
     x, mask = generate_random_case(cfg, 7)
     x2, _ = generate_random_case(cfg, 8)
     xd, md, x2d = x.cuda(), mask.cuda(), x2.cuda()
+    x_keep = xd.clone()
     with torch.inference_mode():
         eager = optimized.OptimizedTransformer.forward(graphed, xd, md).clone()
         outs = [graphed(xd, md).clone() for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 3)]
         assert graphed._graph_states and next(iter(graphed._graph_states.values())).graph is not None
-        other = graphed(x2d, md).clone()  # different tensor: copied into the captured input
+        other = graphed(x2d, md).clone()  # a different input tensor: read directly, no copy
         eager2 = optimized.OptimizedTransformer.forward(graphed, x2d, md)
     for o in outs:
         torch.testing.assert_close(o, eager, atol=0, rtol=0)
     torch.testing.assert_close(other, eager2, atol=0, rtol=0)
+    # the caller's tensors are never written by the replay
+    torch.testing.assert_close(xd, x_keep, atol=0, rtol=0)
+
+
+def test_cuda_graph_replay_with_fresh_equal_masks(cuda_device):
+    """Every call passes a new mask object with the same (padded) lengths and
+    the allocator is churned in between: the captured graph must keep reading
+    the lengths it was captured with, not a freed block."""
+    import cuda_graphs
+
+    cfg = StackConfig(4, 128, 256, 4, 512, 2, True)
+    params = init_params(cfg, seed=0)
+    graphed = cuda_graphs.GraphedTransformer(cfg)
+    graphed.load_state_dict(params, strict=True)
+    graphed = graphed.cuda().eval()
+    x, mask = generate_random_case(cfg, 31, padding_ratio=0.4)
+    assert not bool(mask.all())
+    xd = x.cuda()
+    with torch.inference_mode():
+        eager = optimized.OptimizedTransformer.forward(graphed, xd, mask.cuda()).clone()
+        for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 4):
+            m = mask.clone().cuda()
+            out = graphed(xd, m).clone()
+            del m
+            junk = torch.full((1 << 16,), -7, dtype=torch.int32, device="cuda")  # reuse freed blocks
+            del junk
+            torch.testing.assert_close(out, eager, atol=0, rtol=0)
+    r = compare_outputs(stack_forward(params, cfg, x, mask), out.cpu(), RTOL, ATOL)
+    assert r.passed, str(r)
 
 
 @pytest.mark.parametrize("chunks", [1, 3, 4])

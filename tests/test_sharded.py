@@ -60,8 +60,9 @@ def test_max_over_ranks_without_process_group():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("padding", [0.0, 0.3], ids=["dense", "padded"])
 @pytest.mark.parametrize("mode", ["one_gpu_two_replicas", "all_gpus"])
-def test_sharded_forward_matches_single_gpu(cuda_device, mode):
+def test_sharded_forward_matches_single_gpu(cuda_device, mode, padding):
     import optimized
     from oracle import StackConfig, generate_random_case, init_params
 
@@ -75,17 +76,17 @@ def test_sharded_forward_matches_single_gpu(cuda_device, mode):
     model.load_state_dict(params, strict=True)
     model = model.cuda().eval()
     shard = sharded.ShardedTransformer(model, devices)
-    x, mask = generate_random_case(cfg, 21)
+    x, mask = generate_random_case(cfg, 21, padding_ratio=padding)
     xd, md = x.cuda(), mask.cuda()
     x2, _ = generate_random_case(cfg, 22)
     x2d = x2.cuda()
     with torch.inference_mode():
-        want = model(xd, md)
-        want2 = model(x2d, md)
-        for _ in range(12):  # past graph capture in every replica
-            got = shard(xd, md)
-        got2 = shard(x2d, md).clone()  # replays the captured graphs on new input
-        got_again = shard(xd, md)
+        want = model(xd, md).clone()
+        want2 = model(x2d, md).clone()
+        for _ in range(12):  # past graph capture in every replica; a new mask object every call
+            got = shard(xd, md.clone()).clone()
+        got2 = shard(x2d, md.clone()).clone()  # replays the captured graphs on new input
+        got_again = shard(xd, md.clone()).clone()
         torch.cuda.synchronize()
     torch.testing.assert_close(got, want, atol=0, rtol=0)
     torch.testing.assert_close(got2, want2, atol=0, rtol=0)

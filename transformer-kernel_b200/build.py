@@ -45,37 +45,45 @@ def nvcc() -> str:
 
 
 def kernel_resources(ptxas_log: str) -> dict:
-    """{mangled kernel name: (registers, spill store bytes)} from ptxas -v output."""
-    out, name, spill = {}, None, 0
+    """{mangled kernel name: (registers, spill store bytes, stack frame bytes)}
+    from ptxas -v output. Stack and spill figures are keyed by the function a
+    "Function properties for X" line names (a non-inlined device function's
+    block never counts against the kernel compiled before it); register
+    counts by the entry function being compiled."""
+    regs, frame, entry, props = {}, {}, None, None
     for line in ptxas_log.splitlines():
         m = re.search(r"Compiling entry function '([^']+)'", line)
         if m:
-            name, spill = m.group(1), 0
+            entry, props = m.group(1), None
             continue
-        m = re.search(r"(\d+) bytes spill stores", line)
-        if m and name:
-            spill = int(m.group(1))
+        m = re.search(r"Function properties for (\S+)", line)
+        if m:
+            props = m.group(1)
+            continue
+        m = re.search(r"(\d+) bytes stack frame, (\d+) bytes spill stores", line)
+        if m and props:
+            frame[props] = (int(m.group(2)), int(m.group(1)))
             continue
         m = re.search(r"Used (\d+) registers", line)
-        if m and name:
-            out[name] = (int(m.group(1)), spill)
-            name = None
-    return out
+        if m and entry:
+            regs[entry] = int(m.group(1))
+    return {name: (r, *frame.get(name, (0, 0))) for name, r in regs.items()}
 
 
 def check_register_split(ptxas_log: str) -> None:
     """The persistent attention kernel splits its launch allocation with
     setmaxnreg (csrc/tk_attn.cuh kLaunchRegs): it must build with exactly
-    that many registers per thread and without spills."""
+    that many registers per thread, without spills and without a stack frame
+    (local memory would be reached through the reduced register budget)."""
     text = (HERE / "csrc" / "tk_attn.cuh").read_text()
     want = int(re.search(r"constexpr int kLaunchRegs = (\d+);", text).group(1))
     found = {k: v for k, v in kernel_resources(ptxas_log).items() if "attn15attn_fwd_kernel" in k}
     if not found:
         raise RuntimeError("ptxas output lists no attn_fwd_kernel")
-    bad = {k: v for k, v in found.items() if v != (want, 0)}
+    bad = {k: v for k, v in found.items() if v != (want, 0, 0)}
     if bad:
-        raise RuntimeError(f"attn_fwd_kernel needs {want} registers and no spills for its register split; "
-                           f"ptxas gave (registers, spill bytes) {sorted(bad.values())}")
+        raise RuntimeError(f"attn_fwd_kernel needs {want} registers, no spills and no stack frame for its register "
+                           f"split; ptxas gave (registers, spill bytes, stack bytes) {sorted(bad.values())}")
 
 
 def up_to_date() -> bool:

@@ -240,7 +240,6 @@ int tk_layernorm(const void* x, int x_dtype, int64_t ld_x, const void* y, int y_
   if (!tk_layernorm_supported(d)) return fail(TK_ERR_UNSUPPORTED, "tk_layernorm: d=%lld > 8192", (long long)d);
   if (x == nullptr || gamma == nullptr || beta == nullptr || out == nullptr)
     return fail(TK_ERR_INVALID, "tk_layernorm: null pointer");
-  if (sum_out != nullptr && y == nullptr) return fail(TK_ERR_INVALID, "tk_layernorm: sum_out needs y");
   auto dt_ok = [](int t) { return t == TK_F32 || t == TK_F16; };
   if (!dt_ok(x_dtype) || !dt_ok(out_dtype) || (y != nullptr && !dt_ok(y_dtype)))
     return fail(TK_ERR_INVALID, "tk_layernorm: dtype must be TK_F32 or TK_F16");

@@ -2,6 +2,8 @@
 //
 //   ln     : h = LN(x)                      (reference ln_fwd,     src/fused_kernels.py:164-193)
 //   add_ln : s = x + y (fp32, stored); h = LN(s)   (reference add_ln_fwd, src/fused_kernels.py:196-238)
+//   ln with s : h = LN(x) and s = x (a copy of the input in x's dtype, written
+//            while the row is in registers)
 //
 // Statistics are fp32 and two-pass in registers (mean, then the centred
 // variance), rstd = rsqrtf(var + eps), then the affine and the cast -- the
@@ -77,7 +79,7 @@ struct Vec4<__half> {
 struct Args {
   const void* x;
   const void* y;      // residual branch, may be null
-  void* s;            // x + y, may be null (only meaningful with y)
+  void* s;            // x + y (a copy of x when y is null), may be null
   const float* gamma;
   const float* beta;
   void* h;
@@ -117,8 +119,9 @@ __global__ void __launch_bounds__(256, 3) ln_warp_rows(Args a) {
         Vec4<TY>::load(static_cast<const TY*>(a.y) + row * a.ld_y + c, a.vec, n, w);
 #pragma unroll
         for (int k = 0; k < 4; ++k) v[i][k] = pad ? 0.f : v[i][k] + w[k];
-        if (a.s != nullptr && n > 0) Vec4<TS>::store(static_cast<TS*>(a.s) + row * a.ld_s + c, a.vec, n, v[i]);
       }
+      // s = x + y, or a copy of x when there is no y
+      if (a.s != nullptr && n > 0) Vec4<TS>::store(static_cast<TS*>(a.s) + row * a.ld_s + c, a.vec, n, v[i]);
 #pragma unroll
       for (int k = 0; k < 4; ++k) sum += v[i][k];
     }
@@ -179,8 +182,9 @@ __global__ void __launch_bounds__(256) ln_cta_rows(Args a) {
         Vec4<TY>::load(static_cast<const TY*>(a.y) + row * a.ld_y + c, a.vec, n, w);
 #pragma unroll
         for (int k = 0; k < 4; ++k) v[i][k] = pad ? 0.f : v[i][k] + w[k];
-        if (a.s != nullptr && n > 0) Vec4<TS>::store(static_cast<TS*>(a.s) + row * a.ld_s + c, a.vec, n, v[i]);
       }
+      // s = x + y, or a copy of x when there is no y
+      if (a.s != nullptr && n > 0) Vec4<TS>::store(static_cast<TS*>(a.s) + row * a.ld_s + c, a.vec, n, v[i]);
 #pragma unroll
       for (int k = 0; k < 4; ++k) sum += v[i][k];
     }

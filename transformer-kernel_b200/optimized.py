@@ -159,6 +159,7 @@ class OptimizedTransformer(nn.Module):
         self._weight_cache_key: Optional[tuple] = None
         self._mask_ref: Optional[weakref.ReferenceType] = None
         self._mask_lengths: Optional[torch.Tensor] = None  # None = dense
+        self._mask_key: Optional[tuple] = None
         # Optional launch trace: a list that receives (name, start, end)
         # CUDA events around every kernel launch of the next forwards.
         self.launch_trace: Optional[list] = None
@@ -234,22 +235,28 @@ class OptimizedTransformer(nn.Module):
         (weakref memo, like the reference's ``_mask_is_dense``, :362-389).
         Masks that are not per-row prefixes -- the only kind the harness's
         ``generate_random_case`` makes (:261-271) -- raise."""
+        return self._prefix_lengths_keyed(mask)[0]
+
+    def _prefix_lengths_keyed(self, mask: Optional[torch.Tensor]):
+        """(lengths, key): ``_prefix_lengths`` plus a hashable key of the
+        lengths' values (None when dense), taken at the same sync."""
         if mask is None or self.settings.assume_dense_mask:
-            return None
+            return None, None
         if self._mask_ref is not None and self._mask_ref() is mask:
-            return self._mask_lengths
+            return self._mask_lengths, self._mask_key
         m = mask.to(torch.bool)
         lengths = m.sum(dim=-1, dtype=torch.int32)
         if bool(m.all()):
-            result = None
+            result, key = None, None
         else:
             prefix = torch.arange(m.shape[-1], device=m.device)[None, :] < lengths[:, None]
             if not bool((prefix == m).all()):
                 raise tk.TKError("forward", -2, "valid_token_mask must be a per-row prefix (True then False)")
             result = lengths.contiguous()
+            key = tuple(result.tolist())
         self._mask_ref = weakref.ref(mask)
-        self._mask_lengths = result
-        return result
+        self._mask_lengths, self._mask_key = result, key
+        return result, key
 
     # -- forward --------------------------------------------------------------
     # The forward is opaque to torch.compile (the harness's --compile-user
@@ -259,12 +266,19 @@ class OptimizedTransformer(nn.Module):
     # (src/optimized.py:64-77 keeps its cache builders out for that reason).
     @_outside_compile
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        self._check_input(x)
+        lengths = self._prefix_lengths(valid_token_mask)
+        return self._finish(x, self._run(x, lengths))
+
+    def _check_input(self, x: torch.Tensor) -> None:
         if not x.is_cuda:
             raise tk.TKError("forward", -1, "OptimizedTransformer runs on the B200 kernels only; x must be a CUDA tensor")
         if x.dim() != 3 or x.shape[-1] != self.d_model:
             raise ValueError(f"expected x of shape [B, S, {self.d_model}], got {tuple(x.shape)}")
-        lengths = self._prefix_lengths(valid_token_mask)
-        out = self._run(x, lengths)
+
+    def _finish(self, x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Optional device-error check; the output in x's dtype (the
+        reference casts back too, src/optimized.py:408)."""
         if self.settings.check_device_errors:
             tk.check_device_errors(x.device)
         return out if out.dtype == x.dtype else out.to(x.dtype)
@@ -272,13 +286,7 @@ class OptimizedTransformer(nn.Module):
     def _activations(self, B: int, S: int, d: int, ffn: int, dev: torch.device):
         """Activation buffers of one forward: residual stream fp32 [T, d], h
         fp16 [T, d], qkv fp16 [T, 3d], ctx fp16 [B, S, d], u fp16 [T, ffn] and
-        the output fp32 [T, d]. Fresh from the caching allocator, unless a set
-        for exactly this shape was pinned with `_pin_activations` (graph
-        capture allocates nothing while the stream is capturing)."""
-        key = (B, S, d, ffn, dev)
-        pinned = getattr(self, "_pinned_activations", None)
-        if pinned is not None and pinned[0] == key:
-            return pinned[1]
+        the output fp32 [T, d], from the caching allocator."""
         T = B * S
         return (torch.empty((T, d), dtype=torch.float32, device=dev),
                 torch.empty((T, d), dtype=torch.float16, device=dev),
@@ -287,134 +295,126 @@ class OptimizedTransformer(nn.Module):
                 torch.empty((T, ffn), dtype=torch.float16, device=dev),
                 torch.empty((T, d), dtype=torch.float32, device=dev))
 
-    def _pin_activations(self, x: torch.Tensor):
-        """Allocate and pin the activation buffers for inputs shaped like x
-        (``None`` unpins). Returns the pinned buffers."""
-        if x is None:
-            self._pinned_activations = None
-            return None
+    def _uses_small_stack(self, x: torch.Tensor) -> bool:
+        """Whether a forward over x runs as one tk_stack_small launch."""
         B, S, d = x.shape
         ffn = self.layers[0].ffn_in.weight.shape[0]
-        self._pinned_activations = None
-        bufs = self._activations(B, S, d, ffn, x.device)
-        self._pinned_activations = ((B, S, d, ffn, x.device), bufs)
-        return bufs
+        if not (self.settings.fused_small_stack and tk.lib().tk_stack_small_supported(d, self.num_heads, ffn, S)):
+            return False
+        return bool(self._small_stack_pack(self._weights()))
 
     def _small_stack(self, x, lengths, out, weights) -> Optional[torch.Tensor]:
         """The whole forward in one tk_stack_small launch when the shape and
         settings allow it; None otherwise."""
         B, S, d = x.shape
+        if not self._uses_small_stack(x):
+            return None
         ffn = weights[0].ffn_in_w.shape[0]
-        if not (self.settings.fused_small_stack and
-                tk.lib().tk_stack_small_supported(d, self.num_heads, ffn, S)):
-            return None
-        pack = self._small_stack_pack(weights)
-        if not pack:
-            return None
-        w, vec, eps = pack
+        w, vec, eps = self._small_stack_pack(weights)
         xin = x if (x.dtype == torch.float32 and x.is_contiguous()) else x.to(torch.float32).contiguous()
         if out is None:
-            pinned = getattr(self, "_pinned_activations", None)
-            if pinned is not None and pinned[0] == (B, S, d, ffn, x.device):
-                out = pinned[1][5]  # graph capture: the output buffer was allocated before capture
-            else:
-                out = torch.empty((B, S, d), dtype=torch.float32, device=x.device)
+            out = torch.empty((B, S, d), dtype=torch.float32, device=x.device)
         fg, fb, _ = self._final
-        run = (lambda fn: fn()) if self.launch_trace is None else self._traced("stack_small")
-        run(lambda: tk.call(
+        self._launch("stack_small", lambda: tk.call(
             "tk_stack_small", xin.data_ptr(), out.data_ptr(), w.data_ptr(), vec.data_ptr(), fg.data_ptr(),
             fb.data_ptr(), eps, tk.ptr(lengths), B, S, d, self.num_heads, ffn, len(weights),
             1 if self.config.causal else 0, self.attn_scale, tk.stream_handle(x.device)))
         return out.view(B, S, d)
 
-    def _traced(self, name):
-        def wrap(fn):
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record()
-            result = fn()
-            end.record()
-            self.launch_trace.append((name, start, end))
-            return result
-        return wrap
+    def _launch(self, name, fn, *args, **kwargs):
+        """Run one library call; with ``launch_trace`` set, bracket it with
+        CUDA events on the current stream."""
+        trace = self.launch_trace
+        if trace is None:
+            return fn(*args, **kwargs)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        result = fn(*args, **kwargs)
+        end.record()
+        trace.append((name, start, end))
+        return result
+
+    def _layer_norm(self, src, w, b, eps, dst, lengths=None, seq=0, copy_to=None):
+        """dst = LN(src) over fp32 rows; rows past their prefix length are
+        zeroed when ``lengths`` is given; ``copy_to`` also receives src."""
+        T, d = src.shape
+        tk.call(
+            "tk_layernorm",
+            src.data_ptr(), tk.TK_F32, src.stride(0), None, 0, 0,
+            tk.ptr(copy_to), 0 if copy_to is None else copy_to.stride(0),
+            w.data_ptr(), b.data_ptr(), float(eps),
+            dst.data_ptr(), tk.dtype_code(dst.dtype), dst.stride(0),
+            tk.ptr(lengths), seq, T, d, tk.stream_handle(src.device),
+        )
+
+    def _head(self, x: torch.Tensor, bufs, weights: List[_LayerWeights]) -> None:
+        """First launch of the per-layer forward: h = LN1(x), and the fp32
+        residual stream starts as a copy of x in its own buffer. Only this
+        launch reads the caller's x, so everything after it (``_body``)
+        touches the forward's own buffers alone -- which is what a captured
+        graph replays."""
+        B, S, d = x.shape
+        xin = x.reshape(B * S, d)
+        if xin.dtype != torch.float32 or xin.stride(-1) != 1 or xin.stride(0) != d:
+            xin = xin.to(torch.float32).contiguous()
+        res, h = bufs[0], bufs[1]
+        w0 = weights[0]
+        self._launch("ln", self._layer_norm, xin, w0.norm1_w, w0.norm1_b, w0.norm1_eps, h, copy_to=res)
+
+    def _body(self, B: int, S: int, lengths: Optional[torch.Tensor], bufs, weights: List[_LayerWeights],
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Every launch after ``_head``: the layers (the residual stream is
+        updated in place) and the final LayerNorm into ``out`` (default the
+        forward's own output buffer). Returns the output as [B, S, d]."""
+        res, h, qkv, ctx, u, out_ws = bufs
+        T, d = res.shape
+        ffn = u.shape[1]
+        hd = self.head_dim
+        fused = self.settings.fused_ln_epilogue and tk_linear.fused_ln_supported(d)
+        seq = S if lengths is not None else 0
+        out = out_ws if out is None else out.view(T, d)
+        run, lin = self._launch, tk_linear.linear
+        # q/k/v as [B, H, S, hd] views of the fused projection
+        qkv4 = qkv.view(B, S, 3, self.num_heads, hd)
+        q, k, v = qkv4.permute(2, 0, 3, 1, 4).unbind(0)
+        last = len(weights) - 1
+        for i, w in enumerate(weights):
+            run("gemm_qkv", lin, h, w.qkv_w, w.qkv_b, "bias", out=qkv)
+            run("attn", kernels.flash_attention, q, k, v, self.attn_scale, self.config.causal,
+                kv_len=lengths, out=ctx)
+            ctx2 = ctx.view(T, d)
+            if fused:
+                run("gemm_o_ln", lin, ctx2, w.out_w, w.out_b, "resid_ln", resid=res, sum_out=res,
+                    ln_weight=w.norm2_w, ln_bias=w.norm2_b, eps=w.norm2_eps, out=h)
+            else:
+                run("gemm_o", lin, ctx2, w.out_w, w.out_b, "resid", resid=res, sum_out=res)
+                run("ln", self._layer_norm, res, w.norm2_w, w.norm2_b, w.norm2_eps, h)
+            run("gemm_ffn_in", lin, h, w.ffn_in_w, w.ffn_in_b, "gelu", out=u)
+            if i < last:
+                nw, nb, neps, dst = weights[i + 1].norm1_w, weights[i + 1].norm1_b, weights[i + 1].norm1_eps, h
+            else:
+                nw, nb, neps = self._final
+                dst = out
+            if fused:
+                run("gemm_ffn_out_ln", lin, u, w.ffn_out_w, w.ffn_out_b, "resid_ln", resid=res, sum_out=res,
+                    ln_weight=nw, ln_bias=nb, eps=neps, out=dst, row_len=lengths, seq_len=seq)
+            else:
+                run("gemm_ffn_out", lin, u, w.ffn_out_w, w.ffn_out_b, "resid", resid=res, sum_out=res,
+                    row_len=lengths, seq_len=seq)
+                run("ln", self._layer_norm, res, nw, nb, neps, dst, lengths, seq)
+        return out.view(B, S, d)
 
     def _run(self, x: torch.Tensor, lengths: Optional[torch.Tensor], out: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, S, d = x.shape
-        T = B * S
         dev = x.device
         weights = self._weights()
         with torch.cuda.device(dev):
             fused = self._small_stack(x, lengths, out, weights)
-        if fused is not None:
-            return fused
-        ffn = weights[0].ffn_in_w.shape[0]
-        hd = self.head_dim
-        fused = self.settings.fused_ln_epilogue and tk_linear.fused_ln_supported(d)
-        xin = x.reshape(T, d)
-        if xin.dtype != torch.float32 or xin.stride(-1) != 1 or xin.stride(0) != d:
-            xin = xin.to(torch.float32).contiguous()
-        seq = S if lengths is not None else 0
-
-        res, h, qkv, ctx, u, out_ws = self._activations(B, S, d, ffn, dev)
-        out = out_ws if out is None else out.view(T, d)
-        stream = tk.stream_handle(dev)
-
-        def layer_norm(src, w, b, eps, dst, zero_padded):
-            tk.call(
-                "tk_layernorm",
-                src.data_ptr(), tk.TK_F32, src.stride(0), None, 0, 0, None, 0,
-                w.data_ptr(), b.data_ptr(), float(eps),
-                dst.data_ptr(), tk.dtype_code(dst.dtype), dst.stride(0),
-                tk.ptr(lengths) if zero_padded else None, seq if zero_padded else 0,
-                T, d, stream,
-            )
-
-        trace = self.launch_trace
-
-        def run(name, fn, *args, **kwargs):
-            if trace is None:
-                return fn(*args, **kwargs)
-            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            start.record()
-            result = fn(*args, **kwargs)
-            end.record()
-            trace.append((name, start, end))
-            return result
-
-        lin = tk_linear.linear
-        with torch.cuda.device(dev):
-            w0 = weights[0]
-            run("ln", layer_norm, xin, w0.norm1_w, w0.norm1_b, w0.norm1_eps, h, False)
-            resid = xin
-            # q/k/v as [B, H, S, hd] views of the fused projection
-            qkv4 = qkv.view(B, S, 3, self.num_heads, hd)
-            q, k, v = qkv4.permute(2, 0, 3, 1, 4).unbind(0)
-            last = len(weights) - 1
-            for i, w in enumerate(weights):
-                run("gemm_qkv", lin, h, w.qkv_w, w.qkv_b, "bias", out=qkv)
-                run("attn", kernels.flash_attention, q, k, v, self.attn_scale, self.config.causal,
-                    kv_len=lengths, out=ctx)
-                ctx2 = ctx.view(T, d)
-                if fused:
-                    run("gemm_o_ln", lin, ctx2, w.out_w, w.out_b, "resid_ln", resid=resid, sum_out=res,
-                        ln_weight=w.norm2_w, ln_bias=w.norm2_b, eps=w.norm2_eps, out=h)
-                else:
-                    run("gemm_o", lin, ctx2, w.out_w, w.out_b, "resid", resid=resid, sum_out=res)
-                    run("ln", layer_norm, res, w.norm2_w, w.norm2_b, w.norm2_eps, h, False)
-                resid = res
-                run("gemm_ffn_in", lin, h, w.ffn_in_w, w.ffn_in_b, "gelu", out=u)
-                if i < last:
-                    nw, nb, neps, dst = weights[i + 1].norm1_w, weights[i + 1].norm1_b, weights[i + 1].norm1_eps, h
-                else:
-                    nw, nb, neps = self._final
-                    dst = out
-                if fused:
-                    run("gemm_ffn_out_ln", lin, u, w.ffn_out_w, w.ffn_out_b, "resid_ln", resid=res, sum_out=res,
-                        ln_weight=nw, ln_bias=nb, eps=neps, out=dst, row_len=lengths, seq_len=seq)
-                else:
-                    run("gemm_ffn_out", lin, u, w.ffn_out_w, w.ffn_out_b, "resid", resid=res, sum_out=res,
-                        row_len=lengths, seq_len=seq)
-                    run("ln", layer_norm, res, nw, nb, neps, dst, lengths is not None)
-        return out.view(B, S, d)
+            if fused is not None:
+                return fused
+            bufs = self._activations(B, S, d, weights[0].ffn_in_w.shape[0], dev)
+            self._head(x, bufs, weights)
+            return self._body(B, S, lengths, bufs, weights, out)
 
     # -- host-streamed forward --------------------------------------------------
     @_outside_compile
@@ -429,13 +429,23 @@ class OptimizedTransformer(nn.Module):
         """Forward over a batch that lives in (pinned) host memory.
 
         The batch is cut into ``chunks`` slices of whole sequences (rows are
-        independent, so slicing is exact). Three streams overlap the H2D
-        copy of slice i+1, the forward of slice i and the D2H copy of slice
-        i-1 -- the copy engines and the SMs work at the same time, where the
-        reference's out-of-core runner copies and computes in turn
-        (``src/run_case14.py:286-298``). Returns ``out_host`` (fp32, pinned);
-        it is complete once the current CUDA stream reaches the point where
-        this call returned (synchronise before reading it on the host).
+        independent, so slicing is exact). Three internal streams overlap the
+        H2D copy of a slice, the forward of the one before it and the D2H copy
+        of the one before that -- the copy engines and the SMs work at the
+        same time, where the reference's out-of-core runner copies and
+        computes in turn (``src/run_case14.py:286-298``). Two slots of device
+        buffers alternate, also across calls, and each slot is guarded by its
+        own events, so consecutive calls pipeline into one another: the next
+        call's first copy and forward start while this call's last slice is
+        still being copied back. Dense slices replay a CUDA graph captured per
+        (slot, slice size).
+
+        Returns ``out_host`` (fp32, pinned). It is complete once the current
+        CUDA stream reaches the point where this call returned (synchronise
+        before reading it on the host). The internal streams order themselves
+        after the caller's stream only for the weight copies and prefix
+        lengths this call builds; x_host is read asynchronously, so it must
+        not be rewritten before the call's work has completed.
         """
         if x_host.is_cuda:
             raise ValueError("forward_from_host takes a host tensor; use forward() for device tensors")
@@ -449,53 +459,91 @@ class OptimizedTransformer(nn.Module):
             x_host = x_host.float()
         if out_host is None:
             out_host = torch.empty((B, S, d), dtype=torch.float32, pin_memory=True)
-        lengths = self._prefix_lengths(valid_token_mask)
+        caller = torch.cuda.current_stream(dev)
+        cache_before = self._weight_cache
+        with torch.cuda.device(dev):
+            weights = self._weights()
+        lengths, _ = self._prefix_lengths_keyed(valid_token_mask)
         if lengths is not None:
             lengths = lengths.to(dev)
         n = max(1, min(int(chunks), B))
         bounds = [B * i // n for i in range(n + 1)]
         cb = max(bounds[i + 1] - bounds[i] for i in range(n))
-        key = (dev, S, d, cb)
-        ctx = getattr(self, "_stream_ctx", None)
-        if ctx is None or ctx["key"] != key:
-            with torch.cuda.device(dev):
-                ctx = {
-                    "key": key,
-                    "h2d": torch.cuda.Stream(dev),
-                    "d2h": torch.cuda.Stream(dev),
-                    "x": [torch.empty((cb, S, d), dtype=torch.float32, device=dev) for _ in range(2)],
-                    "out": [torch.empty((cb, S, d), dtype=torch.float32, device=dev) for _ in range(2)],
-                    "in_ready": [torch.cuda.Event() for _ in range(2)],
-                    "computed": [torch.cuda.Event() for _ in range(2)],
-                    "out_free": [torch.cuda.Event() for _ in range(2)],
-                }
-            self._stream_ctx = ctx
-        compute = torch.cuda.current_stream(dev)
-        h2d, d2h = ctx["h2d"], ctx["d2h"]
-        # slots may still be in use by a previous call on the compute stream
-        h2d.wait_stream(compute)
-        d2h.wait_stream(compute)
+        ctx = self._stream_context(dev, S, d, cb, weights)
+        h2d, compute, d2h = ctx["h2d"], ctx["compute"], ctx["d2h"]
+        if self._weight_cache is not cache_before or (lengths is not None and lengths is not ctx["lengths"]):
+            # weight copies / lengths were just built on the caller's stream
+            ready = torch.cuda.Event()
+            ready.record(caller)
+            compute.wait_event(ready)
+            ctx["lengths"] = lengths
         with torch.cuda.device(dev):
             for i in range(n):
-                s, b0, b1 = i % 2, bounds[i], bounds[i + 1]
+                s = ctx["next_slot"]
+                ctx["next_slot"] ^= 1
+                b0, b1 = bounds[i], bounds[i + 1]
                 nb = b1 - b0
-                xs, os_ = ctx["x"][s][:nb], ctx["out"][s][:nb]
+                slot = ctx["slots"][s]
+                xs, os_ = slot["x"][:nb], slot["out"][:nb]
                 with torch.cuda.stream(h2d):
-                    if i >= 2:
-                        h2d.wait_event(ctx["computed"][s])  # forward i-2 done reading the slot
+                    h2d.wait_event(slot["computed"])   # the last forward that read this input slot is done
                     xs.copy_(x_host[b0:b1], non_blocking=True)
-                    ctx["in_ready"][s].record(h2d)
-                compute.wait_event(ctx["in_ready"][s])
-                if i >= 2:
-                    compute.wait_event(ctx["out_free"][s])  # D2H i-2 done reading the slot
-                self._run(xs, None if lengths is None else lengths[b0:b1], out=os_)
-                ctx["computed"][s].record(compute)
+                    slot["in_ready"].record(h2d)
+                compute.wait_event(slot["in_ready"])
+                compute.wait_event(slot["out_free"])   # the last D2H that read this output slot is done
+                with torch.cuda.stream(compute):
+                    self._slot_forward(slot, xs, os_, None if lengths is None else lengths[b0:b1], weights)
+                slot["computed"].record(compute)
                 with torch.cuda.stream(d2h):
-                    d2h.wait_event(ctx["computed"][s])
+                    d2h.wait_event(slot["computed"])
                     out_host[b0:b1].copy_(os_, non_blocking=True)
-                    ctx["out_free"][s].record(d2h)
-            compute.wait_stream(d2h)
-            compute.wait_stream(h2d)
+                    slot["out_free"].record(d2h)
+            caller.wait_stream(d2h)
         if self.settings.check_device_errors:
             tk.check_device_errors(dev)
         return out_host
+
+    def _stream_context(self, dev, S, d, cb, weights):
+        """Streams, two slots of device buffers (input, output, activations)
+        and their events for ``forward_from_host``; rebuilt when the slice
+        shape changes."""
+        key = (dev, S, d, cb)
+        ctx = getattr(self, "_stream_ctx", None)
+        if ctx is not None and ctx["key"] == key:
+            return ctx
+        ffn = weights[0].ffn_in_w.shape[0]
+        with torch.cuda.device(dev):
+            slots = [{"x": torch.empty((cb, S, d), dtype=torch.float32, device=dev),
+                      "out": torch.empty((cb, S, d), dtype=torch.float32, device=dev),
+                      "bufs": self._activations(cb, S, d, ffn, dev),
+                      "graphs": {},
+                      "in_ready": torch.cuda.Event(), "computed": torch.cuda.Event(),
+                      "out_free": torch.cuda.Event()} for _ in range(2)]
+            ctx = {"key": key, "h2d": torch.cuda.Stream(dev), "compute": torch.cuda.Stream(dev),
+                   "d2h": torch.cuda.Stream(dev), "slots": slots, "next_slot": 0, "lengths": None}
+        self._stream_ctx = ctx
+        return ctx
+
+    def _slot_forward(self, slot, xs, os_, lengths, weights) -> None:
+        """Forward of one slice on the current stream: slot buffers in, slot
+        output out. Dense slices of the per-layer path replay a graph captured
+        per slice size on the second use (everything they touch is the slot's
+        own); padded slices and one-launch shapes run eagerly."""
+        nb, S, d = xs.shape
+        if lengths is not None or self._uses_small_stack(xs):
+            self._run(xs, lengths, out=os_)
+            return
+        bufs = tuple(b[:nb * S] if b.dim() == 2 else b[:nb] for b in slot["bufs"])
+        g = slot["graphs"].get(nb)
+        if g is None:
+            self._head(xs, bufs, weights)
+            self._body(nb, S, None, bufs, weights, out=os_)
+            slot["graphs"][nb] = "warm"
+            return
+        if g == "warm":
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=xs.device)):
+                self._head(xs, bufs, weights)
+                self._body(nb, S, None, bufs, weights, out=os_)
+            slot["graphs"][nb] = g = graph
+        g.replay()

@@ -59,8 +59,10 @@ class ShardedTransformer(torch.nn.Module):
     ``OptimizedTransformer`` (on ``devices[0]``) and builds graph-replayed
     replicas on the other devices (weights copied once). ``forward(x,
     valid_token_mask=None)`` takes ``x`` on ``devices[0]`` and returns the
-    full ``[B, S, d]`` output there. A device may be listed more than once
-    (replicas on one GPU; used to test the split/gather logic on one GPU).
+    full ``[B, S, d]`` fp32 output there. The returned tensor is reused by
+    the next call with the same shape (like ``GraphedTransformer``'s output);
+    clone it to keep it. A device may be listed more than once (replicas on
+    one GPU; used to test the split/gather logic on one GPU).
     """
 
     def __init__(self, model: optimized.OptimizedTransformer, devices: Sequence) -> None:
@@ -76,20 +78,40 @@ class ShardedTransformer(torch.nn.Module):
             rep.load_state_dict({k: v.to(dev) for k, v in state.items()}, strict=True)
             self.replicas.append(rep.to(dev).eval())
         self.streams = [torch.cuda.Stream(device=d) for d in devices]
+        # per-shard streams on the first device: a cross-device copy runs on
+        # the source device's current stream, so each shard's scatter gets its
+        # own stream there and the shards' copies run side by side
+        self.home_streams = [torch.cuda.Stream(device=devices[0]) for _ in devices]
         self._bufs = {}
+        self._lengths = {}  # (shard, lengths key) -> that shard's prefix lengths on its device
         self._mask_owner = self.replicas[0]  # its dense-mask memo (one sync per mask object)
 
     def _shard_buffers(self, x: torch.Tensor, bounds):
         key = (tuple(x.shape), x.dtype)
         bufs = self._bufs.get(key)
         if bufs is None:
-            bufs = []
+            inputs = []
             for (b0, b1), dev in zip(bounds, self.devices):
-                shape = (b1 - b0,) + tuple(x.shape[1:])
-                bufs.append((torch.empty(shape, dtype=torch.float32, device=dev),
-                             torch.empty(shape, dtype=torch.float32, device=dev)))
+                inputs.append(torch.empty((b1 - b0,) + tuple(x.shape[1:]), dtype=torch.float32, device=dev))
+            out = torch.empty(x.shape, dtype=torch.float32, device=self.devices[0])
+            bufs = (inputs, out)
             self._bufs = {key: bufs}
         return bufs
+
+    def _shard_lengths(self, r: int, lengths: Optional[torch.Tensor], lkey, b0: int, b1: int):
+        """Shard r's prefix lengths on its device, built once per distinct
+        lengths from the host-side key by a blocking host-to-device copy, so
+        no stream ordering is involved."""
+        if lengths is None:
+            return None, None
+        key = (r, lkey)
+        got = self._lengths.get(key)
+        if got is None:
+            if len(self._lengths) > 64:
+                self._lengths.clear()
+            got = (torch.tensor(lkey[b0:b1], dtype=torch.int32, device=self.devices[r]), lkey[b0:b1])
+            self._lengths[key] = got
+        return got
 
     @optimized._outside_compile
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -99,9 +121,8 @@ class ShardedTransformer(torch.nn.Module):
         n = len(self.devices)
         B = x.shape[0]
         bounds = [shard_bounds(B, n, r) for r in range(n)]
-        out = torch.empty(x.shape, dtype=torch.float32, device=home)
-        bufs = self._shard_buffers(x, bounds)
-        dense = self._mask_owner._prefix_lengths(valid_token_mask) is None
+        inputs, out = self._shard_buffers(x, bounds)
+        lengths, lkey = self._mask_owner._prefix_lengths_keyed(valid_token_mask)
         main = torch.cuda.current_stream(home)
         ready = torch.cuda.Event()
         ready.record(main)
@@ -110,18 +131,22 @@ class ShardedTransformer(torch.nn.Module):
             b0, b1 = bounds[r]
             if b1 == b0:
                 continue
-            xin, yout = bufs[r]
-            mask = None if dense else valid_token_mask[b0:b1].to(dev, non_blocking=True)
-            with torch.cuda.device(dev), torch.cuda.stream(stream):
+            xin = inputs[r]
+            len_r, lkey_r = self._shard_lengths(r, lengths, lkey, b0, b1)
+            hs = self.home_streams[r]
+            hs.wait_event(ready)
+            # Nested stream contexts make hs the first device's current stream
+            # and `stream` the shard device's, so torch runs the scatter on hs
+            # (source side) and the gather on `stream` (source side), and
+            # makes the other side wait for each copy.
+            with torch.cuda.stream(hs), torch.cuda.stream(stream):
                 stream.wait_event(ready)
                 xin.copy_(x[b0:b1], non_blocking=True)        # scatter (peer copy over NVLink)
-                y = self.replicas[r](xin, mask)
-                yout.copy_(y, non_blocking=True)
+                y = self.replicas[r]._forward_lengths(xin, len_r, lkey_r)
+                out[b0:b1].copy_(y, non_blocking=True)        # gather onto the first device
                 ev = torch.cuda.Event()
                 ev.record(stream)
-            done.append((r, ev))
-        for r, ev in done:
-            b0, b1 = bounds[r]
+            done.append(ev)
+        for ev in done:
             main.wait_event(ev)
-            out[b0:b1].copy_(bufs[r][1], non_blocking=True)   # gather onto the first device
         return out
