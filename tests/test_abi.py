@@ -82,8 +82,8 @@ def test_layernorm_rejects_bad_arguments_on_host():
     lib = tk.lib()
     assert lib.tk_layernorm(16, 0, 64, None, 0, 0, None, 0, 16, 16, 1e-5, 16, 1, 64, None, 0, 4, 9000, None) == -2
     assert lib.tk_layernorm(None, 0, 64, None, 0, 0, None, 0, 16, 16, 1e-5, 16, 1, 64, None, 0, 4, 64, None) == -1
-    # sum_out without a residual
-    assert lib.tk_layernorm(16, 0, 64, None, 0, 0, 16, 64, 16, 16, 1e-5, 16, 1, 64, None, 0, 4, 64, None) == -1
+    # a copy-through sum_out whose row stride is shorter than a row
+    assert lib.tk_layernorm(16, 0, 64, None, 0, 0, 16, 32, 16, 16, 1e-5, 16, 1, 64, None, 0, 4, 64, None) == -1
 
 
 def test_python_wrappers_refuse_cpu_tensors():
