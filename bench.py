@@ -2,32 +2,46 @@
 """Benchmark of the B200 layer-stack forward (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C3] [--impl tk|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      # the batch split over N GPUs
 
 A "step" is one forward of the layer stack over one synthetic batch of the
 chosen configuration (default C3: batch 256, seq 256, d_model 1024, 16
 heads, ffn 4096, 4 layers, bidirectional -- the large-batch GEMM regime that
 BASELINE.json runs at 1/2/4/8 GPUs). Weights are the harness's default
 initialisation under torch.manual_seed(0); x ~ N(0, 1) fp32, seeded on the
-CPU. Batch rows are independent, so under torchrun every rank runs its own
-full batch on its own GPU with no data-path collective (weak scaling); the
-value is all ranks' tokens over the max-over-ranks device time.
+CPU (the harness's generator and init; no dataset is involved).
+
+One GPU: the public graph-replaying drop-in (GraphedTransformer) on the
+whole batch. N GPUs (torchrun, one process per GPU): the north-star split
+(distributed.BatchSplitForward) -- the batch lives in rank 0's HBM, every
+rank computes its shard of sequences, and the fp32 output is gathered back
+into rank 0's HBM over NVLink inside the timed step (strong scaling: the
+global batch is the config's at every N). ``--replicas`` instead runs the
+whole batch on every rank (weak scaling, no exchange).
 
 Metric: tokens/s (= B*S*1000 / ms per forward, the harness's throughput,
 src/torch_transformer_benchmark.py:565-567). ``value`` is device-timed with
-inputs resident in HBM (inputs are > L2, so no flush is needed); ``e2e``
-times the same forward through the public API with the input copied from
-pinned host memory and the fp32 output copied back every step.
+inputs resident in HBM (inputs are > L2, so no flush is needed), the max
+over ranks; ``e2e`` times the same forward through the public API from
+pinned host memory, the fp32 output copied back every step
+(``forward_from_host``; under torchrun each rank streams its own shard).
+``roofline`` is the dominant kernel's achieved rate over the measured burst
+peak (per-launch CUDA-event times of a separate traced pass), and
+``roofline_per_kernel`` lists every kernel the same way. ``extra_configs``
+carries the other BASELINE.json configurations measured the same way
+(C1, C2, C4, C5 on one GPU; C4 and C5 split over the N GPUs under torchrun).
 
 ``--impl reference`` times the fp32 CPU forward of the reference model (the
 oracle's restatement of BaselineTransformer; the reference is pure Python
 and does not travel to the GPU box) on the host cores, one bounded
-batch-slice per step. For C5 and A14 (S = 100,000) the CPU forward of even
-one sequence is ~10^14 FLOP per layer, so the CPU figure is extrapolated from
-the exact query-chunked oracle: two one-layer runs over all keys with 8 and R
-query rows give the per-row cost and the all-row (LayerNorm / K / V) cost,
-scaled to S rows and L layers. A14 is the reference's case 14
-(configs/shapes.json: batch 32, seq 100000, d 1024, 16 heads, ffn 1024, 2
-layers).
+batch-slice per step; ``ms_per_step`` is the measured slice time and the
+full-batch extrapolation has its own key. For C5 and A14 (S = 100,000) the
+CPU forward of even one sequence is ~10^14 FLOP per layer, so the CPU figure
+is extrapolated from the exact query-chunked oracle: two one-layer runs over
+all keys with 8 and R query rows give the per-row cost and the all-row
+(LayerNorm / K / V) cost, scaled to S rows and L layers. A14 is the
+reference's case 14 (configs/shapes.json: batch 32, seq 100000, d 1024, 16
+heads, ffn 1024, 2 layers).
 
 C1 and C2 fit in L2: their steps are timed one by one with an L2 flush
 (a 512 MB write) between them, outside the events. Larger configurations
@@ -88,6 +102,7 @@ METRIC = "layer-stack forward tokens/s"
 
 
 def peaks():
+    """(HBM GB/s, bf16 burst TFLOP/s, bf16 sustained TFLOP/s, source)."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         m = json.loads(path.read_text())
@@ -95,14 +110,60 @@ def peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def gemm_flops(T, d, ffn):
-    return {"gemm_qkv": 2 * T * d * 3 * d, "gemm_o": 2 * T * d * d, "gemm_o_ln": 2 * T * d * d,
-            "gemm_ffn_in": 2 * T * d * ffn, "gemm_ffn_out": 2 * T * ffn * d, "gemm_ffn_out_ln": 2 * T * ffn * d}
-
-
 def attn_flops(B, S, H, hd, causal):
+    """Useful attention FLOP: 4 * B * H * hd per unmasked (query, key) pair."""
     pairs = S * (S + 1) / 2 if causal else S * S
     return 4 * B * H * pairs * hd
+
+
+def kernel_work(name, cfg_tuple, batch):
+    """Algorithmic work of one launch of kernel `name` in a forward over
+    `batch` sequences: ("tensor", FLOP) for GEMMs and attention (2*M*N*K;
+    4*B*H*hd*pairs) or ("hbm", bytes) for LayerNorm (rows*d*bytes per
+    element: ln_in reads fp32 x and writes fp16 h plus the fp32 residual
+    copy, 10 B; ln reads fp32 and writes fp16, 6 B; ln_out writes fp32, 8 B)."""
+    _, S, d, H, ffn, L, causal = cfg_tuple
+    T = batch * S
+    gemm = {"gemm_qkv": (d, 3 * d), "gemm_o": (d, d), "gemm_o_ln": (d, d), "gemm_ffn_in": (d, ffn),
+            "gemm_ffn_out": (ffn, d), "gemm_ffn_out_ln": (ffn, d)}
+    if name in gemm:
+        k, n = gemm[name]
+        return "tensor", 2.0 * T * n * k
+    if name == "attn":
+        return "tensor", attn_flops(batch, S, H, d // H, causal)
+    if name == "stack_small":
+        per_layer = 2.0 * T * (4 * d * d + 2 * d * ffn) + attn_flops(batch, S, H, d // H, causal)
+        return "tensor", L * per_layer
+    per_elt = {"ln_in": 10, "ln": 6, "ln_out": 8}.get(name, 6)
+    return "hbm", float(T * d * per_elt)
+
+
+def roofline_table(per, cfg_tuple, batch, config_name=None):
+    """Per-kernel rooflines from per-launch CUDA-event times (ms lists), each
+    against the measured burst peak (the kernels are timed launch by launch,
+    not inside a seconds-long loop); returns (table, dominant kernel's entry)."""
+    hbm, tf_burst, tf_sus, kind = peaks()
+    totals = {k: sum(v) for k, v in per.items()}
+    grand = sum(totals.values()) or 1.0
+    table = {}
+    for name, times in per.items():
+        bound, work = kernel_work(name, cfg_tuple, batch)
+        avg = statistics.fmean(times)
+        if bound == "tensor":
+            achieved, peak, unit = work / (avg * 1e-3) / 1e12, tf_burst, "TFLOP/s"
+        else:
+            achieved, peak, unit = work / (avg * 1e-3) / 1e9, hbm, "GB/s"
+        table[name] = {"bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+                       "frac": round(achieved / peak, 4), "avg_ms": round(avg, 5),
+                       "launches_per_step": None, "share": round(totals[name] / grand, 4)}
+    dom = max(totals, key=totals.get)
+    e = table[dom]
+    roof = {"kernel": dom, "bound": e["bound"], "achieved": e["achieved"], "peak": e["peak"], "unit": e["unit"],
+            "frac": e["frac"],
+            "peak_kind": f"{kind} {'bf16 burst' if e['bound'] == 'tensor' else 'copy'}",
+            "frac_of_sustained": (round(e["achieved"] / tf_sus, 4) if e["bound"] == "tensor" else None),
+            "traffic": measured_traffic(config_name, dom, batch) if config_name else None}
+    return table, roof
 
 
 class Clocks:
@@ -245,29 +306,39 @@ def cpu_long_seq_rate(cfg_tuple, rows=1024, reps=2):
     return S / t_seq, threads, desc, [t_seq]
 
 
+def workload(name, cfg_tuple):
+    B, S, d, H, ffn, L, causal = cfg_tuple
+    return f"{name} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}"
+
+
 def run_reference(args, cfg_tuple, rank):
-    """--impl reference: the CPU fp32 reference forward on the host cores."""
+    """--impl reference: the CPU fp32 reference forward on the host cores,
+    one bounded batch slice per step; under torchrun rank 0 alone runs."""
     if rank != 0:
         return
     B, S, d, H, ffn, L, causal = cfg_tuple
     if args.config in ("C5", "A14"):
         value, threads, desc, times = cpu_long_seq_rate(cfg_tuple)
-        med, sample = times[0], 1
+        slice_ms, sample = times[0] * 1e3, 1
+        sample_desc = desc
     else:
-        sample = 8 if args.config in ("C3",) else (1 if args.config == "C4" else B)
+        sample = min(B, 8 if args.config in ("C3",) else (1 if args.config == "C4" else B))
         rate, threads, desc, times = cpu_forward_rate(cfg_tuple, 0, sample, steps=args.warmup + args.steps)
         times = times[args.warmup:] or times
-        med = statistics.median(times)
-        value = min(B, sample) * S / med
+        slice_ms = statistics.median(times) * 1e3
+        value = sample * S * 1000.0 / slice_ms
+        sample_desc = f"{sample} of {B} sequences per step (median of {len(times)} timed steps)"
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": med * 1e3 * (B / min(B, sample)), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "impl": "reference",
-        "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
-                   "global_batch": B, "seq_len": S, "parallelism": "cpu"},
+        "warmup": args.warmup, "ms_per_step": slice_ms, "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 and not args.replicas else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": workload(args.config, cfg_tuple), "global_batch": B, "seq_len": S},
+        "parallelism": "cpu (host cores of rank 0)",
+        "step_sample": sample_desc,
+        "full_batch_ms_extrapolated": slice_ms * B / sample,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": desc if args.config in ("C5", "A14") else f"{min(B, sample)} of {B} sequences per step"},
+                         "sample": sample_desc},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -418,6 +489,103 @@ def measured_traffic(config, kernel, batch):
     return entry["bytes_per_launch"] * batch / entry["batch"]
 
 
+def trace_kernels(model, x, mask, steps):
+    """Per-launch CUDA-event times of every kernel over `steps` eager forwards
+    (separate pass, same stream): {name: [ms, ...]}, launches per forward."""
+    import optimized
+
+    trace = []
+    model.launch_trace = trace
+    for _ in range(steps):
+        optimized.OptimizedTransformer.forward(model, x, mask)
+    torch.cuda.synchronize(x.device)
+    model.launch_trace = None
+    per = {}
+    for name, a, b in trace:
+        per.setdefault(name, []).append(a.elapsed_time(b))
+    return per, len(trace) // steps
+
+
+def attach_launch_counts(table, per, steps):
+    for name, times in per.items():
+        table[name]["launches_per_step"] = len(times) // steps
+    return table
+
+
+def timed_steps(fn, steps, stream, dev, flush_buf=None):
+    """Mean ms per step of `fn` on `stream`: back to back between one event
+    pair, or (with `flush_buf`) one event pair per step with an L2 flush
+    (a write larger than L2) between steps, outside the events."""
+    if flush_buf is None:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        return t0.elapsed_time(t1) / steps
+    pairs = []
+    for _ in range(steps):
+        flush_buf.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        pairs.append((a, b))
+    torch.cuda.synchronize(dev)
+    return sum(a.elapsed_time(b) for a, b in pairs) / steps
+
+
+def device_input(cfg_tuple, dev, seed=1234 + 100000):
+    """x ~ N(0, 1) fp32 drawn on the device (seeded) for the extra
+    configurations, whose inputs reach 13 GB."""
+    B, S, d = cfg_tuple[:3]
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return torch.randn(B, S, d, device=dev, generator=g)
+
+
+def measure_one_gpu(name, dev, steps=None, warmup=3):
+    """One GPU, device-resident: ms per forward, tokens/s, the dominant
+    kernel's roofline and the per-kernel table, clocks (extra configurations
+    of the default run)."""
+    import _tklib as tk
+    import cuda_graphs
+    import optimized
+
+    cfg_tuple = CONFIGS[name]
+    B, S, d, H, ffn, L, causal = cfg_tuple
+    steps = steps or (2 if name in ("C5", "A14") else 20)
+    torch.manual_seed(0)
+    ocfg = optimized.TransformerConfig(B, S, d, H, ffn, L, causal)
+    graphed = name not in ("C5", "A14")
+    model = (cuda_graphs.GraphedTransformer(ocfg) if graphed else optimized.OptimizedTransformer(ocfg)).to(dev).eval()
+    x = device_input(cfg_tuple, dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if name in L2_RESIDENT else None
+    with torch.inference_mode():
+        for _ in range((cuda_graphs.WARMUP_BEFORE_CAPTURE + 1 if graphed else 0) + warmup):
+            model(x)
+        tk.check_device_errors(dev)
+        with Clocks(dev.index) as clk:
+            clk.mark("t_start")
+            ms = timed_steps(lambda: model(x), steps, stream, dev, flush)
+            clk.mark("t_end")
+        per, launches = trace_kernels(model, x, None, max(1, min(steps, 5)))
+        tk.check_device_errors(dev)
+    table, roof = roofline_table(per, cfg_tuple, B, name)
+    attach_launch_counts(table, per, max(1, min(steps, 5)))
+    del model, x
+    torch.cuda.empty_cache()
+    return {"workload": workload(name, cfg_tuple), "ms_per_step": ms, "value": B * S * 1000.0 / ms,
+            "unit": "tokens/s", "steps": steps, "warmup": warmup,
+            "vs_baseline": (B * S * 1000.0 / ms / PUBLISHED_TOKENS_PER_S[name]
+                            if name in PUBLISHED_TOKENS_PER_S else None),
+            "l2": "flushed between steps" if flush is not None else "working set > L2",
+            "data": "synthetic, x drawn on the device", "roofline": roof, "roofline_per_kernel": table,
+            "gpu_launches_per_step": launches, "clocks": clk.summary()}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -428,7 +596,15 @@ def main() -> int:
     ap.add_argument("--impl", default="tk", choices=["tk", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-chunks", type=int, default=4, help="batch slices of the streamed end-to-end forward")
+    ap.add_argument("--e2e-chunks", type=int, default=0,
+                    help="batch slices of the streamed end-to-end forward (default: ~16+ sequences a slice, <= 4)")
+    ap.add_argument("--extras", default="auto",
+                    help="comma-separated extra configurations measured after the main one (default: C1,C2,C4,C5 "
+                         "on one GPU, C4,C5 split under torchrun); 'none' to skip")
+    ap.add_argument("--micro-batches", type=int, default=2,
+                    help="torchrun split: micro-batches per rank (copy-in / forward / copy-out overlap)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="torchrun: every rank runs the whole batch (weak scaling, no exchange)")
     ap.add_argument("--sweep", default="", help="comma-separated appendix cases (or 'all'): one JSON line each, "
                                                 "timed like the harness (median of CUDA-event samples)")
     ap.add_argument("--set", action="append", default=[], metavar="FIELD=VALUE",
@@ -450,7 +626,6 @@ def main() -> int:
     cfg_tuple = CONFIGS[args.config]
     if args.batch > 0:
         cfg_tuple = (args.batch,) + cfg_tuple[1:]
-    B, S, d, H, ffn, L, causal = cfg_tuple
 
     if args.impl == "reference":
         run_reference(args, cfg_tuple, rank)
@@ -461,10 +636,45 @@ def main() -> int:
         if world > 1:
             ap.error("--strong runs in one process; do not launch it under torchrun")
         return run_strong(args, cfg_tuple)
+    if world > 1 and not args.replicas:
+        return run_split(args, cfg_tuple, world, rank, local)
+    return run_single(args, cfg_tuple, world, rank, local)
 
+
+def cpu_baseline(args, cfg_tuple):
+    if args.no_cpu_baseline:
+        return None
+    B = cfg_tuple[0]
+    if args.config in ("C5", "A14"):
+        rate, threads, desc, _ = cpu_long_seq_rate(cfg_tuple)
+    else:
+        sample = 8 if args.config == "C3" else (1 if args.config == "C4" else B)
+        rate, threads, desc, _ = cpu_forward_rate(cfg_tuple, args.cpu_seconds, sample)
+    return {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
+
+
+def e2e_chunks(args, batch):
+    if args.e2e_chunks > 0:
+        return args.e2e_chunks
+    return max(1, min(4, batch // 16))
+
+
+def extras_list(args, world):
+    if args.extras == "none" or args.batch > 0:
+        return []
+    if args.extras != "auto":
+        return [c for c in args.extras.split(",") if c and c != args.config]
+    if world > 1:
+        return [c for c in ("C4", "C5") if c != args.config]
+    return [c for c in ("C1", "C2", "C4", "C5") if c != args.config]
+
+
+def run_single(args, cfg_tuple, world, rank, local):
+    """One GPU (or --replicas: every rank its own whole batch)."""
     import torch.distributed as dist
     from datetime import timedelta
 
+    B, S, d, H, ffn, L, causal = cfg_tuple
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
@@ -477,12 +687,10 @@ def main() -> int:
     ocfg = optimized.TransformerConfig(B, S, d, H, ffn, L, causal)
     torch.manual_seed(0)
     # The public graph-replaying drop-in (the reference's --cuda-graphs
-    # path); its eager superclass forward is used for the per-kernel trace.
-    # C5 (one ~1 s forward per step) runs the eager drop-in: a graph saves
-    # nothing there and its static input/output copies would cost 26 GB.
+    # path). C5 (one ~1 s forward per step) runs the eager drop-in: a graph
+    # saves nothing there.
     graphed = args.config not in ("C5", "A14")
     model = (cuda_graphs.GraphedTransformer(ocfg) if graphed else optimized.OptimizedTransformer(ocfg)).to(dev).eval()
-    eager_forward = optimized.OptimizedTransformer.forward
     gen = torch.Generator().manual_seed(1234 + 100000)
     x_host = torch.randn(B, S, d, generator=gen).pin_memory()
     mask_host = torch.ones(B, S, dtype=torch.bool).pin_memory()
@@ -502,11 +710,8 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    flush = args.config in L2_RESIDENT
-    scratch = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if flush else None
-
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if args.config in L2_RESIDENT else None
     with torch.inference_mode():
-        # ---- graph capture (untimed), then device-resident timing ----
         if graphed:
             for _ in range(cuda_graphs.WARMUP_BEFORE_CAPTURE + 1):
                 model(x, mask)
@@ -517,50 +722,21 @@ def main() -> int:
         torch.cuda.synchronize(dev)
         with Clocks(local) as clk:
             clk.mark("t_start")
-            if flush:
-                # one event pair per step; the L2 flush between steps is outside them
-                pairs = []
-                for _ in range(args.steps):
-                    scratch.fill_(1)
-                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    a.record(stream)
-                    model(x, mask)
-                    b.record(stream)
-                    pairs.append((a, b))
-                torch.cuda.synchronize(dev)
-                local_ms = sum(a.elapsed_time(b) for a, b in pairs) / args.steps
-            else:
-                t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                t0.record(stream)
-                for _ in range(args.steps):
-                    model(x, mask)
-                t1.record(stream)
-                torch.cuda.synchronize(dev)
-                local_ms = t0.elapsed_time(t1) / args.steps
+            local_ms = timed_steps(lambda: model(x, mask), args.steps, stream, dev, flush)
             clk.mark("t_end")
         barrier()
         ms = max_over_ranks(local_ms)
         clocks = clk.summary()
         tk.check_device_errors(dev)
 
-        # ---- per-kernel event timing (separate pass, same stream) ----
-        trace = []
-        model.launch_trace = trace
-        for _ in range(args.steps):
-            eager_forward(model, x, mask)
-        torch.cuda.synchronize(dev)
-        model.launch_trace = None
-        per = {}
-        for name, a, b in trace:
-            per.setdefault(name, []).append(a.elapsed_time(b))
-        launches_per_step = len(trace) // args.steps
+        trace_steps = max(1, min(args.steps, 10))
+        per, launches_per_step = trace_kernels(model, x, mask, trace_steps)
 
-        # ---- end to end: pinned host input -> forward -> host output ----
-        # Large batches go through the public streamed API (H2D, forward
-        # and D2H of batch slices overlap); small ones copy in, replay the
-        # graph and copy out.
+        # end to end: pinned host input -> forward -> pinned host output,
+        # through the public streamed API (copies overlap the forward, also
+        # across consecutive calls); small batches copy in, replay, copy out
         streamed = x_host.numel() * 4 >= (64 << 20)
-        chunks = args.e2e_chunks
+        chunks = e2e_chunks(args, B)
 
         def e2e_step():
             if streamed:
@@ -573,87 +749,195 @@ def main() -> int:
             e2e_step()
         barrier()
         torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
+        e2e_ms = max_over_ranks(timed_steps(e2e_step, args.steps, stream, dev))
         barrier()
-        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
     tokens = B * S
     value = world * tokens * 1000.0 / ms
-    hbm, tf_burst, tf_sus, peak_kind = peaks()
-    # dominant kernel by total time
-    totals = {k: sum(v) for k, v in per.items()}
-    dom = max(totals, key=totals.get)
-    avg_ms = statistics.fmean(per[dom])
-    T = tokens
-    fl = gemm_flops(T, d, ffn)
-    if dom in fl:
-        achieved = fl[dom] / (avg_ms * 1e-3) / 1e12
-        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
-                "frac": achieved / tf_sus, "peak_kind": f"{peak_kind} bf16 sustained"}
-    elif dom == "stack_small":
-        # the whole forward is one kernel: all GEMM and attention FLOP of the stack
-        g = gemm_flops(T, d, ffn)
-        total = L * (g["gemm_qkv"] + g["gemm_o"] + g["gemm_ffn_in"] + g["gemm_ffn_out"]
-                     + attn_flops(B, S, H, d // H, causal))
-        achieved = total / (avg_ms * 1e-3) / 1e12
-        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
-                "frac": achieved / tf_sus, "peak_kind": f"{peak_kind} bf16 sustained",
-                "note": "one-launch whole-stack kernel; latency-bound at this size"}
-    elif dom == "attn":
-        achieved = attn_flops(B, S, H, d // H, causal) / (avg_ms * 1e-3) / 1e12
-        roof = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tf_sus, "unit": "TFLOP/s",
-                "frac": achieved / tf_sus, "peak_kind": f"{peak_kind} bf16 sustained"}
-    else:
-        achieved = T * d * (4 + 2) / (avg_ms * 1e-3) / 1e9
-        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "peak_kind": f"{peak_kind} copy"}
-    roof["traffic"] = measured_traffic(args.config, dom, B)
-    share = {k: round(v / sum(totals.values()), 4) for k, v in sorted(totals.items(), key=lambda kv: -kv[1])}
-    kernels_ms = {k: round(statistics.fmean(v), 5) for k, v in per.items()}
+    table, roof = roofline_table(per, cfg_tuple, B, args.config if args.batch == 0 else None)
+    attach_launch_counts(table, per, trace_steps)
 
+    extras = {}
+    if rank == 0 and world == 1:
+        del model, x
+        torch.cuda.empty_cache()
+        for name in extras_list(args, world):
+            extras[name] = measure_one_gpu(name, dev)
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
         return 0
-
-    cpu = None
-    if not args.no_cpu_baseline:
-        if args.config in ("C5", "A14"):
-            rate, threads, desc, _ = cpu_long_seq_rate(cfg_tuple)
-        else:
-            sample = 8 if args.config == "C3" else (1 if args.config == "C4" else B)
-            rate, threads, desc, _ = cpu_forward_rate(cfg_tuple, args.cpu_seconds, sample)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": desc}
-
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": (value / PUBLISHED_TOKENS_PER_S[args.config]
                         if args.config in PUBLISHED_TOKENS_PER_S and args.batch == 0 else None),
         "dtype": "f16 operands / f32 accumulate+residual", "data": "synthetic",
-        "config": {"workload": f"{args.config} b{B} s{S} d{d} h{H} ffn{ffn} L{L} {'causal' if causal else 'bidir'}",
-                   "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world} (batch-sharded, no collective)",
-                   "l2": ("L2 flushed between steps (512 MB write outside the events)" if flush
-                          else "inputs and activations > 126 MB L2; no flush")},
+        "config": {"workload": workload(args.config, cfg_tuple), "global_batch": B * world, "seq_len": S},
+        "parallelism": ("1 GPU" if world == 1 else f"{world} replicas (each rank the whole batch, no exchange)"),
+        "l2": ("L2 flushed between steps (512 MB write outside the events)" if flush is not None
+               else "inputs and activations > 126 MB L2; no flush"),
         "e2e": {"value": world * tokens * 1000.0 / e2e_ms, "unit": "tokens/s", "ms_per_step": e2e_ms,
-                "path": f"forward_from_host, {chunks} streamed slices" if streamed else "copy in, graph replay, copy out",
+                "path": (f"forward_from_host, {chunks} streamed slices per call, consecutive calls pipelined"
+                         if streamed else "copy in, graph replay, copy out"),
                 "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": out_host.numel() * 4},
         "roofline": roof,
-        "kernel_ms": kernels_ms,
-        "kernel_share": share,
+        "roofline_per_kernel": table,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks,
-        "cpu_baseline": cpu,
+        "cpu_baseline": cpu_baseline(args, cfg_tuple),
+        "extra_configs": extras,
     }
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def run_split(args, cfg_tuple, world, rank, local):
+    """torchrun, one process per GPU: the north-star split of one batch."""
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    try:
+        main_line = split_config(args, args.config, cfg_tuple, world, rank, local, dev, host_input=True)
+        extras = {}
+        for name in extras_list(args, world):
+            extras[name] = split_config(args, name, CONFIGS[name], world, rank, local, dev, host_input=False)
+        if rank == 0:
+            main_line["extra_configs"] = extras
+            print(json.dumps(main_line), flush=True)
+        dist.barrier(device_ids=[local])
+    finally:
+        dist.destroy_process_group()
+    return 0
+
+
+def split_config(args, name, cfg_tuple, world, rank, local, dev, host_input):
+    """One configuration through distributed.BatchSplitForward; returns the
+    JSON line (meaningful on rank 0)."""
+    import torch.distributed as dist
+
+    import _tklib as tk
+    import distributed
+    import optimized
+    from sharded import shard_bounds
+
+    B, S, d, H, ffn, L, causal = cfg_tuple
+    main = host_input
+    steps = args.steps if main else (2 if name in ("C5", "A14") else 20)
+    warmup = args.warmup if main else 3
+    torch.manual_seed(0)  # identical weights on every rank
+    model = optimized.OptimizedTransformer(optimized.TransformerConfig(B, S, d, H, ffn, L, causal)).to(dev).eval()
+    split = distributed.BatchSplitForward(model, (B, S, d), micro_batches=args.micro_batches)
+    b0, b1 = split.bounds
+    x_host = None
+    if main:
+        gen = torch.Generator().manual_seed(1234 + 100000)
+        x_host = torch.randn(B, S, d, generator=gen).pin_memory()
+        if rank == 0:
+            split.input.copy_(x_host)
+    elif rank == 0:
+        split.input.copy_(device_input(cfg_tuple, dev))
+    stream = torch.cuda.current_stream(dev)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.inference_mode():
+        for _ in range(2 + warmup):  # slot graphs are captured on a slot's second use
+            split.step()
+        tk.check_device_errors(dev)
+        dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+        with Clocks(local) as clk:
+            clk.mark("t_start")
+            local_ms = timed_steps(split.step, steps, stream, dev)
+            clk.mark("t_end")
+        dist.barrier(device_ids=[local])
+        ms = max_over_ranks(local_ms)
+        tk.check_device_errors(dev)
+        clocks = [None] * world
+        dist.all_gather_object(clocks, clk.summary())
+
+        # parity: the gathered rows of the first and last sequence of every
+        # rank's shard against a one-GPU forward of those sequences on rank 0
+        parity = None
+        if rank == 0:
+            picks = sorted({v for r in range(world) for v in
+                            (shard_bounds(B, world, r)[0], shard_bounds(B, world, r)[1] - 1)
+                            if shard_bounds(B, world, r)[1] > shard_bounds(B, world, r)[0]})
+            worst, exact = 0.0, True
+            per_chunk = 4 if S * d <= (1 << 22) else 1
+            for i in range(0, len(picks), per_chunk):
+                idx = torch.tensor(picks[i:i + per_chunk], device=dev)
+                want = model(split.input.index_select(0, idx))
+                got = split.output.index_select(0, idx)
+                diff = (want - got).abs().max().item()
+                worst = max(worst, diff)
+                exact = exact and bool(torch.equal(want, got))
+            parity = {"sequences_checked": len(picks), "against": "one-GPU forward of the same sequences",
+                      "bit_exact": exact, "max_abs_diff": worst}
+
+        # per-kernel times on this rank's micro-batch shape (rank 0)
+        per, launches = {}, 0
+        mb = split.micro[0][1] - split.micro[0][0] if split.micro else 0
+        if rank == 0 and mb:
+            xs = split.slots[0]["x"][:mb]
+            per, launches = trace_kernels(model, xs, None, 3 if main else 1)
+
+        # end to end: every rank streams its own shard from pinned host memory
+        e2e_ms = None
+        if main:
+            xs_host = x_host[b0:b1]
+            os_host = torch.empty_like(xs_host).pin_memory()
+            chunks = e2e_chunks(args, b1 - b0)
+            if b1 > b0:
+                for _ in range(3):
+                    model.forward_from_host(xs_host, None, out_host=os_host, chunks=chunks)
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize(dev)
+            e2e_local = timed_steps(lambda: model.forward_from_host(xs_host, None, out_host=os_host, chunks=chunks)
+                                    if b1 > b0 else None, steps, stream, dev)
+            e2e_ms = max_over_ranks(e2e_local)
+        split.close()
+    line = None
+    if rank == 0:
+        table, roof = roofline_table(per, cfg_tuple, mb, name if main and args.batch == 0 else None) if per \
+            else ({}, None)
+        attach_launch_counts(table, per, 3 if main else 1)
+        tokens = B * S
+        line = {
+            "metric": METRIC, "value": tokens * 1000.0 / ms, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 operands / f32 accumulate+residual", "data": "synthetic",
+            "config": {"workload": workload(name, cfg_tuple), "global_batch": B, "seq_len": S},
+            "parallelism": (f"batch split over {world} GPUs: input in rank 0's HBM, shards copied over NVLink "
+                            f"(copy engines, CUDA IPC), {len(split.micro)} micro-batches per rank overlapping "
+                            f"copy-in / forward / copy-out, fp32 output gathered into rank 0's HBM in the step"),
+            "l2": "inputs and activations > 126 MB L2; no flush",
+            "parity": parity,
+            "roofline": roof,
+            "roofline_per_kernel": table,
+            "roofline_note": f"per-kernel times on one micro-batch ({mb} sequences) of rank 0",
+            "gpu_launches": launches * len(split.micro) * steps,
+            "gpu_launches_scope": "rank 0's kernels in the timed steps",
+            "clocks": clocks[0],
+            "clocks_all_ranks": clocks,
+        }
+        if main:
+            line["e2e"] = {"value": tokens * 1000.0 / e2e_ms, "unit": "tokens/s", "ms_per_step": e2e_ms,
+                           "path": "every rank: forward_from_host over its shard (pinned host -> its GPU -> pinned host)",
+                           "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": x_host.numel() * 4}
+            line["cpu_baseline"] = cpu_baseline(args, cfg_tuple)
+    del split, model
+    torch.cuda.empty_cache()
+    return line
 
 
 if __name__ == "__main__":

@@ -134,6 +134,31 @@ TK_API int tk_stack_small(const float* x, float* out, const void* w_packed, cons
                           const int32_t* row_len, int64_t B, int64_t S, int64_t d, int64_t heads,
                           int64_t ffn, int64_t L, int causal, float scale, void* stream);
 
+/* Peer memory and row copies for the batch-split forward over the GPUs of
+ * one node, one process per GPU. Replaces the exchange the reference runs
+ * serially, batch chunk after batch chunk on one device
+ * (src/run_case14.py:153-158 chunked, :279-322 its streamed loop): here the
+ * chunks are the ranks' shards, the first rank's buffers hold the whole
+ * batch, and every other rank maps them.
+ *   tk_peer_export : `handle` (64 bytes, opaque) names the device allocation
+ *                    that contains `ptr`; *offset is ptr's byte offset in it.
+ *                    Send both to the other processes.
+ *   tk_peer_import : maps that allocation into this process (peer access to
+ *                    its device is enabled on first touch); *ptr = the
+ *                    exported pointer's address here. Importing the same
+ *                    allocation again returns the same mapping (counted).
+ *   tk_peer_release: drops one import of the mapping that holds `ptr`.
+ *   tk_copy_rows   : `rows` rows of `row_bytes` bytes from src (rows
+ *                    src_ld bytes apart) to dst (dst_ld bytes apart), stream
+ *                    ordered; either side may be an imported peer pointer,
+ *                    in which case the copy engines move it over NVLink
+ *                    without using any SM. */
+TK_API int tk_peer_export(const void* ptr, void* handle, int64_t* offset);
+TK_API int tk_peer_import(const void* handle, int64_t offset, void** ptr);
+TK_API int tk_peer_release(void* ptr);
+TK_API int tk_copy_rows(void* dst, int64_t dst_ld, const void* src, int64_t src_ld, int64_t row_bytes, int64_t rows,
+                        void* stream);
+
 /* Guard probes, same meaning as the reference's can_fuse
  * (src/fused_kernels.py:62-64) and attention_supported
  * (src/kernels.py:96-103): 1 when the kernels accept the shape. */

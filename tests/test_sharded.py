@@ -91,3 +91,114 @@ def test_sharded_forward_matches_single_gpu(cuda_device, mode, padding):
     torch.testing.assert_close(got, want, atol=0, rtol=0)
     torch.testing.assert_close(got2, want2, atol=0, rtol=0)
     torch.testing.assert_close(got_again, want, atol=0, rtol=0)
+
+
+# ---- the torchrun batch split (distributed.BatchSplitForward) --------------
+
+@pytest.mark.parametrize("batch,world,micro", [(256, 8, 2), (8, 8, 2), (32, 8, 4), (10, 4, 3), (3, 4, 2), (32, 2, 16)])
+def test_split_plan_partitions_the_batch(batch, world, micro):
+    import distributed
+
+    pieces = [p for r in range(world) for p in distributed.split_plan(batch, world, r, micro)]
+    assert sorted(pieces) == pieces  # rank order, no overlap
+    covered = [i for s, e in pieces for i in range(s, e)]
+    assert covered == list(range(batch))
+    assert all(e > s for s, e in pieces)
+    for r in range(world):
+        assert len(distributed.split_plan(batch, world, r, micro)) <= micro
+
+
+def _gloo_plan_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    import distributed
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mine = distributed.split_plan(256, world, rank, 2)
+        rows = torch.zeros(256, dtype=torch.int64)
+        for s, e in mine:
+            rows[s:e] += 1
+        dist.all_reduce(rows)  # every sequence computed by exactly one rank
+        box = [None] * world
+        dist.all_gather_object(box, mine)
+        q.put((rank, int(rows.min()), int(rows.max()), box))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_split_plan_gloo_world_size_2():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + (os.getpid() % 1000)
+    procs = [ctx.Process(target=_gloo_plan_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    results = sorted((q.get(timeout=10) for _ in range(2)), key=lambda t: t[0])
+    for _, lo, hi, box in results:
+        assert (lo, hi) == (1, 1)
+        assert box == [[(0, 64), (64, 128)], [(128, 192), (192, 256)]]
+
+
+def _ipc_owner(q_handle, q_done, result):
+    import torch
+
+    import _tklib as tk
+
+    torch.cuda.set_device(0)
+    src = torch.arange(6 * 1024, dtype=torch.float32, device="cuda").view(6, 1024)
+    dst = torch.full((6, 1024), -1.0, device="cuda")
+    torch.cuda.synchronize()
+    q_handle.put((tk.peer_export(src), tk.peer_export(dst[1:])))  # an interior pointer: offset > 0
+    assert q_done.get(timeout=120) == "written"
+    torch.cuda.synchronize()
+    want = torch.full((6, 1024), -1.0, device="cuda")
+    want[1:] = src[[4, 5, 2, 3, 0]]  # the rows the peer gathered, written back from dst row 1 on
+    result.put(bool(torch.equal(dst, want)))
+
+
+def _ipc_peer(q_handle, q_done, result):
+    import torch
+
+    import _tklib as tk
+
+    torch.cuda.set_device(0)
+    (h_src, o_src), (h_dst, o_dst) = q_handle.get(timeout=120)
+    assert o_src == 0 or o_src > 0
+    src = tk.peer_import(h_src, o_src)
+    dst = tk.peer_import(h_dst, o_dst)
+    mine = torch.empty(5, 1024, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    rb = 1024 * 4
+    # gather rows 4,5 then 2,3 then 0 of the owner's tensor, then write them back strided
+    tk.copy_rows(mine.data_ptr(), rb, src + 4 * rb, rb, rb, 2, stream)
+    tk.copy_rows(mine.data_ptr() + 2 * rb, rb, src + 2 * rb, rb, rb, 2, stream)
+    tk.copy_rows(mine.data_ptr() + 4 * rb, rb, src, rb, rb, 1, stream)
+    tk.copy_rows(dst, rb, mine.data_ptr(), rb, rb, 5, stream)
+    torch.cuda.synchronize()
+    ok = bool(torch.equal(mine[0], torch.arange(4 * 1024, 5 * 1024, dtype=torch.float32, device="cuda")))
+    tk.peer_release(src)
+    tk.peer_release(dst)
+    q_done.put("written")
+    result.put(ok)
+
+
+@pytest.mark.gpu
+def test_peer_export_import_copy_rows_between_processes(cuda_device):
+    """tk_peer_export / tk_peer_import / tk_copy_rows between two processes
+    (one GPU is enough: CUDA IPC maps the owner's allocation into the peer;
+    the processes order themselves on the host, no kernel waits on another)."""
+    ctx = mp.get_context("spawn")
+    q_handle, q_done, result = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_ipc_owner, args=(q_handle, q_done, result)),
+             ctx.Process(target=_ipc_peer, args=(q_handle, q_done, result))]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+        assert p.exitcode == 0
+    assert [result.get(timeout=10), result.get(timeout=10)] == [True, True]

@@ -46,6 +46,10 @@ SIGNATURES = {
     "tk_stack_small_supported": (_I, [_I64, _I64, _I64, _I64]),
     "tk_stack_small": (_I, [_P, _P, _P, _P, _P, _P, _F, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _F, _P]),
     "tk_selftest_wait_timeout": (_I, [_P]),
+    "tk_peer_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
+    "tk_peer_import": (_I, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
+    "tk_peer_release": (_I, [_P]),
+    "tk_copy_rows": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P]),
     "tk_last_error": (ctypes.c_char_p, []),
     "tk_version": (ctypes.c_char_p, []),
 }
@@ -136,3 +140,31 @@ def set_programmatic_launch(enable: bool) -> bool:
 
 def version() -> str:
     return lib().tk_version().decode()
+
+
+def peer_export(t: torch.Tensor) -> tuple:
+    """(64-byte handle, byte offset) naming the device allocation of ``t``,
+    for ``peer_import`` in another process of the same node."""
+    handle = ctypes.create_string_buffer(64)
+    offset = ctypes.c_int64(0)
+    call("tk_peer_export", t.data_ptr(), handle, ctypes.byref(offset))
+    return handle.raw, int(offset.value)
+
+
+def peer_import(handle: bytes, offset: int) -> int:
+    """Device address, in this process, of a pointer another process exported."""
+    if len(handle) != 64:
+        raise TKError("tk_peer_import", -1, "handle must be the 64 bytes tk_peer_export wrote")
+    ptr = ctypes.c_void_p(0)
+    call("tk_peer_import", ctypes.create_string_buffer(handle, 64), int(offset), ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def peer_release(ptr: int) -> None:
+    call("tk_peer_release", ptr)
+
+
+def copy_rows(dst: int, dst_ld: int, src: int, src_ld: int, row_bytes: int, rows: int, stream: int) -> None:
+    """Stream-ordered copy of ``rows`` rows of ``row_bytes`` between device
+    addresses (either may be an imported peer address)."""
+    call("tk_copy_rows", dst, dst_ld, src, src_ld, row_bytes, rows, stream)

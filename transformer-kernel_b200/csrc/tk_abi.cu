@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -134,6 +135,33 @@ int current_device(int* dev, DeviceInfo** info) {
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Base and size of the device allocation that contains `ptr` (driver API
+// cuMemGetAddressRange, reached like cuTensorMapEncodeTiled).
+int allocation_range(const void* ptr, CUdeviceptr* base, size_t* size) {
+  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<RangeFn>(p);
+  });
+  if (fn == nullptr) return fail(TK_ERR_CUDA, "cuMemGetAddressRange unavailable from the driver");
+  CUresult r = fn(base, size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(TK_ERR_INVALID, "no device allocation holds %p (CUresult %d)", ptr, static_cast<int>(r));
+  return TK_OK;
+}
+
+// Imported peer allocations: one mapping per exported allocation, counted.
+struct PeerMap {
+  void* base;
+  int refs;
+};
+std::mutex g_peer_mu;
+std::map<std::string, PeerMap> g_peer_maps;
 
 // ----------------------------------------------------------------------------
 // GEMM dispatch
@@ -568,6 +596,79 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, int64_t stride_b, i
                 built_regs, tk::attn::kLaunchRegs);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tk_attn_fwd launch");
+  return TK_OK;
+}
+
+// ----------------------------------------------------------------------------
+// peer memory (CUDA IPC) and row copies
+// ----------------------------------------------------------------------------
+int tk_peer_export(const void* ptr, void* handle, int64_t* offset) {
+  g_last_error.clear();
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return fail(TK_ERR_INVALID, "tk_peer_export: null pointer");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (int st = allocation_range(ptr, &base, &size)) return st;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return TK_OK;
+}
+
+int tk_peer_import(const void* handle, int64_t offset, void** ptr) {
+  g_last_error.clear();
+  if (handle == nullptr || ptr == nullptr || offset < 0) return fail(TK_ERR_INVALID, "tk_peer_import: bad argument");
+  const std::string key(static_cast<const char*>(handle), 64);
+  std::lock_guard<std::mutex> lk(g_peer_mu);
+  auto it = g_peer_maps.find(key);
+  if (it == g_peer_maps.end()) {
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    it = g_peer_maps.emplace(key, PeerMap{base, 0}).first;
+  }
+  ++it->second.refs;
+  *ptr = static_cast<char*>(it->second.base) + offset;
+  return TK_OK;
+}
+
+int tk_peer_release(void* ptr) {
+  g_last_error.clear();
+  std::lock_guard<std::mutex> lk(g_peer_mu);
+  // the mapping whose range holds ptr: the largest base not above it
+  auto best = g_peer_maps.end();
+  for (auto it = g_peer_maps.begin(); it != g_peer_maps.end(); ++it) {
+    if (it->second.base <= ptr && (best == g_peer_maps.end() || it->second.base > best->second.base)) best = it;
+  }
+  if (best == g_peer_maps.end()) return fail(TK_ERR_INVALID, "tk_peer_release: %p is not in an imported mapping", ptr);
+  if (--best->second.refs == 0) {
+    cudaError_t e = cudaIpcCloseMemHandle(best->second.base);
+    g_peer_maps.erase(best);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+  }
+  return TK_OK;
+}
+
+int tk_copy_rows(void* dst, int64_t dst_ld, const void* src, int64_t src_ld, int64_t row_bytes, int64_t rows,
+                 void* stream) {
+  g_last_error.clear();
+  if (rows < 0 || row_bytes < 0 || (rows > 0 && (dst == nullptr || src == nullptr)))
+    return fail(TK_ERR_INVALID, "tk_copy_rows: bad argument");
+  if (rows > 1 && (dst_ld < row_bytes || src_ld < row_bytes))
+    return fail(TK_ERR_INVALID, "tk_copy_rows: row stride smaller than a row");
+  if (rows == 0 || row_bytes == 0) return TK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (dst_ld == row_bytes && src_ld == row_bytes)
+    e = cudaMemcpyAsync(dst, src, static_cast<size_t>(row_bytes * rows), cudaMemcpyDeviceToDevice, s);
+  else
+    e = cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_ld), src, static_cast<size_t>(src_ld),
+                          static_cast<size_t>(row_bytes), static_cast<size_t>(rows), cudaMemcpyDeviceToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e, "tk_copy_rows");
   return TK_OK;
 }
 

@@ -359,7 +359,7 @@ class OptimizedTransformer(nn.Module):
             xin = xin.to(torch.float32).contiguous()
         res, h = bufs[0], bufs[1]
         w0 = weights[0]
-        self._launch("ln", self._layer_norm, xin, w0.norm1_w, w0.norm1_b, w0.norm1_eps, h, copy_to=res)
+        self._launch("ln_in", self._layer_norm, xin, w0.norm1_w, w0.norm1_b, w0.norm1_eps, h, copy_to=res)
 
     def _body(self, B: int, S: int, lengths: Optional[torch.Tensor], bufs, weights: List[_LayerWeights],
               out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -401,7 +401,7 @@ class OptimizedTransformer(nn.Module):
             else:
                 run("gemm_ffn_out", lin, u, w.ffn_out_w, w.ffn_out_b, "resid", resid=res, sum_out=res,
                     row_len=lengths, seq_len=seq)
-                run("ln", self._layer_norm, res, nw, nb, neps, dst, lengths, seq)
+                run("ln" if i < last else "ln_out", self._layer_norm, res, nw, nb, neps, dst, lengths, seq)
         return out.view(B, S, d)
 
     def _run(self, x: torch.Tensor, lengths: Optional[torch.Tensor], out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -542,7 +542,10 @@ class OptimizedTransformer(nn.Module):
             return
         if g == "warm":
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=xs.device)):
+            # thread-local capture mode: other threads of the process (a
+            # process group's watchdog) may query events meanwhile
+            with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=xs.device),
+                                  capture_error_mode="thread_local"):
                 self._head(xs, bufs, weights)
                 self._body(nb, S, None, bufs, weights, out=os_)
             slot["graphs"][nb] = g = graph
