@@ -130,7 +130,8 @@ def test_batch_rows_are_independent(cuda_device):
 def test_cuda_graph_replay_matches_eager(cuda_device):
     import cuda_graphs
 
-    cfg = StackConfig(8, 128, 128, 4, 128, 2, True)
+    # a per-layer shape (the one-launch small-shape kernel is not captured)
+    cfg = StackConfig(8, 128, 256, 4, 512, 2, True)
     params = init_params(cfg, seed=0)
     graphed = cuda_graphs.GraphedTransformer(cfg)
     graphed.load_state_dict(params, strict=True)
