@@ -91,6 +91,32 @@ TK_API int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw,
             const int32_t* row_len, int64_t seq_len,
             int64_t M, int64_t N, int64_t K, void* stream);
 
+/* GEMM + bias + residual add + LayerNorm for any row width up to 4096:
+ *   sum_out = resid + A W^T + bias (fp32, may be in place: sum_out == resid)
+ *   out     = LN(sum_out) * gamma + beta (fp16 or fp32, statistics in fp32)
+ * Replaces F.linear (src/optimized.py:627, :632-636) followed by add_ln_fwd
+ * (src/fused_kernels.py:196-238), which the reference fuses for any
+ * d_model <= 8192 with its Triton kernel. N in {64, 128, 256} runs
+ * tk_gemm's TK_EPI_BIAS_RESID_LN (one tile holds the row; the workspace is
+ * unused). N % 256 == 0 with 512 <= N <= 4096 runs the CTA-pair GEMM, whose
+ * epilogue publishes per-row partial statistics of each 128-column slice to
+ * `workspace`; the last slice of a row to arrive triggers that row's
+ * normalisation. The workspace is tk_gemm_resid_ln_workspace_bytes(M, N)
+ * bytes (or more), 256-byte aligned, owned by the caller, and must be zero
+ * before its first use; every call that completes leaves it as it found it
+ * (after a reported device error, zero it again). A workspace sized for M
+ * rows serves any call with at most M rows. Calls that share a workspace
+ * must not overlap on the GPU. Other arguments as tk_gemm. */
+TK_API int64_t tk_gemm_resid_ln_workspace_bytes(int64_t M, int64_t N);
+TK_API int tk_gemm_resid_ln_supported(int64_t M, int64_t N, int64_t K);
+TK_API int tk_gemm_resid_ln(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                            const float* resid, int64_t ld_resid, float* sum_out, int64_t ld_sum,
+                            const float* gamma, const float* beta, float eps,
+                            void* out, int out_dtype, int64_t ldo,
+                            const int32_t* row_len, int64_t seq_len,
+                            int64_t M, int64_t N, int64_t K,
+                            void* workspace, int64_t workspace_bytes, void* stream);
+
 /* Attention forward. Replaces F.scaled_dot_product_attention
  * (src/optimized.py:615-624) and flash_attention (src/kernels.py:250-294),
  * with the same contract as the latter: q, k, v are fp16, logically

@@ -95,3 +95,21 @@ def test_python_wrappers_refuse_cpu_tensors():
     with pytest.raises(tk.TKError):
         fused_kernels.ln_fwd(x, torch.ones(64), torch.zeros(64), 1e-5)
     assert not fused_kernels.can_fuse(x)
+
+
+def test_resid_ln_workspace_and_support_on_host():
+    lib = tk.lib()
+    # one tile holds rows of 64/128/256: no workspace
+    assert lib.tk_gemm_resid_ln_workspace_bytes(65536, 256) == 0
+    # counters [M] u32 + partials [M, N/128] float2, each 256-byte aligned
+    assert lib.tk_gemm_resid_ln_workspace_bytes(65536, 1024) == 65536 * 4 + 65536 * 8 * 8
+    assert lib.tk_gemm_resid_ln_workspace_bytes(1000, 512) == 4096 + 32000
+    assert lib.tk_gemm_resid_ln_supported(65536, 1024, 4096) == 1
+    assert lib.tk_gemm_resid_ln_supported(65536, 640, 4096) == 0   # not a multiple of 256
+    assert lib.tk_gemm_resid_ln_supported(65536, 8192, 4096) == 0  # above 4096
+    assert lib.tk_gemm_resid_ln_supported(65536, 1024, 12) == 0    # K % 8
+    # refused before any launch: unsupported width, missing workspace
+    assert lib.tk_gemm_resid_ln(16, 64, 16, 64, 16, 16, 640, 16, 640, 16, 16, 1e-5, 16, 1, 640, None, 0, 8, 640, 64,
+                                16, 4096, None) == -2
+    assert lib.tk_gemm_resid_ln(16, 64, 16, 64, 16, 16, 1024, 16, 1024, 16, 16, 1e-5, 16, 1, 1024, None, 0, 8, 1024,
+                                64, None, 0, None) == -1

@@ -229,3 +229,87 @@ def test_gemm_pair_resid_out_of_place(cuda_device, row_len):
         got, want = got[~pad], want[~pad]
     torch.testing.assert_close(got, want, atol=1e-4, rtol=1e-4)
     assert torch.equal(rc.cpu(), r)  # resid untouched
+
+
+# ---- residual + LayerNorm over rows wider than a tile (tk_gemm_resid_ln) ----
+# Per-row partial statistics of every 128-column slice in a workspace, the
+# row's last slice normalising it. Same tolerances as the one-tile LN
+# epilogue: fp32 sum 1e-4, fp16 LN output 2e-3/2e-2, fp32 LN output 1e-4.
+
+WIDE_LN = [(65536, 1024, 1024), (4096, 1024, 4096), (300, 512, 200), (1, 768, 64), (5000, 2048, 256),
+           (777, 4096, 512)]
+
+
+def _ln_case(M, N, K, seed):
+    a, w, b = operands(M, N, K, seed=seed)
+    r = seeded(M, N, seed=seed + 3)
+    g = seeded(N, seed=seed + 4, scale=0.5) + 1.0
+    beta = seeded(N, seed=seed + 5, scale=0.5)
+    return a, w, b, r, g, beta
+
+
+@pytest.mark.parametrize("M,N,K", WIDE_LN)
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_gemm_resid_ln_wide_rows(cuda_device, M, N, K, out_dtype):
+    a, w, b, r, g, beta = _ln_case(M, N, K, seed=M + N + K)
+    s, h = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid_ln", resid=r.cuda(), ln_weight=g.cuda(),
+                            ln_bias=beta.cuda(), eps=1e-5, out_dtype=out_dtype)
+    want_s = r + ref_linear(a, w, b)
+    torch.testing.assert_close(s.cpu(), want_s, atol=1e-4, rtol=1e-4)
+    want_h = F.layer_norm(want_s, (N,), g, beta, 1e-5)
+    tol = dict(atol=2e-3, rtol=2e-2) if out_dtype == torch.float16 else dict(atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(h.float().cpu(), want_h, **tol)
+
+
+def test_gemm_resid_ln_in_place_workspace_reuse(cuda_device):
+    """The residual stream updated in place, the same workspace across calls
+    and across row counts (a larger call, then smaller ones, then the larger
+    again): the counters every call leaves at zero keep it reusable."""
+    N, K = 1024, 1024
+    Mbig = 8192
+    ws = torch.zeros(tk_linear.ln_workspace_bytes(Mbig, N), dtype=torch.uint8, device="cuda")
+    for i, M in enumerate([Mbig, 1000, 4097, Mbig]):
+        a, w, b, r, g, beta = _ln_case(M, N, K, seed=100 + i)
+        res = r.cuda()
+        h = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid_ln", resid=res, sum_out=res, ln_weight=g.cuda(),
+                         ln_bias=beta.cuda(), eps=1e-5, out=h, workspace=ws)
+        want_s = r + ref_linear(a, w, b)
+        torch.testing.assert_close(res.cpu(), want_s, atol=1e-4, rtol=1e-4)
+        torch.testing.assert_close(h.float().cpu(), F.layer_norm(want_s, (N,), g, beta, 1e-5), atol=2e-3, rtol=2e-2)
+    torch.cuda.synchronize()
+    count_bytes = (Mbig * 4 + 255) // 256 * 256
+    assert int(ws[:count_bytes].view(torch.int32).abs().sum()) == 0  # every row counter back at zero
+
+
+def test_gemm_resid_ln_row_len_and_large_mean(cuda_device):
+    """Padded rows give s = 0 and h = 0; rows with a large common offset keep
+    the centred statistics (a one-pass E[x^2] - E[x]^2 would lose them)."""
+    S, B, N, K = 256, 24, 1024, 256
+    M = B * S
+    a, w, b, r, g, beta = _ln_case(M, N, K, seed=71)
+    r = r + 300.0
+    lengths = (torch.arange(B, dtype=torch.int32) * 41) % (S + 1)
+    s, h = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid_ln", resid=r.cuda(), ln_weight=g.cuda(),
+                            ln_bias=beta.cuda(), eps=1e-5, out_dtype=torch.float32, row_len=lengths.cuda(), seq_len=S)
+    pad = (torch.arange(M) % S) >= lengths.repeat_interleave(S)
+    got_s, got_h = s.cpu(), h.cpu()
+    assert torch.all(got_s[pad] == 0) and torch.all(got_h[pad] == 0)
+    want_s = r + ref_linear(a, w, b)
+    torch.testing.assert_close(got_s[~pad], want_s[~pad], atol=1e-4, rtol=1e-4)
+    want_h = F.layer_norm(want_s, (N,), g, beta, 1e-5)
+    torch.testing.assert_close(got_h[~pad], want_h[~pad], atol=1e-3, rtol=1e-3)
+
+
+def test_gemm_resid_ln_rejects_bad_workspace(cuda_device):
+    import _tklib as tk
+
+    M, N, K = 512, 1024, 256
+    a, w, b, r, g, beta = _ln_case(M, N, K, seed=81)
+    small = torch.zeros(tk_linear.ln_workspace_bytes(M, N) - 256, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError):
+        tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid_ln", resid=r.cuda(), ln_weight=g.cuda(),
+                         ln_bias=beta.cuda(), workspace=small)
+    rc = tk.lib().tk_gemm_resid_ln(16, K, 16, K, 16, 16, N, 16, N, 16, 16, 1e-5, 16, 1, N, None, 0, M, N, K,
+                                   None, 0, None)
+    assert rc == -1 and b"workspace" in tk.lib().tk_last_error()

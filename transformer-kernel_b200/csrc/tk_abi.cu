@@ -108,7 +108,7 @@ int make_map_f16(CUtensorMap* map, const void* base, int rank, const cuuint64_t*
 
 struct DeviceInfo {
   int sms = 0;
-  bool gemm_attr_set[4][4] = {};
+  bool gemm_attr_set[4][5] = {};
   bool attn_attr_set[5] = {};
   bool small_attr_set[2] = {};
 };
@@ -424,6 +424,89 @@ int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
     case 256: return launch_gemm_epi<256>(epilogue, ma, mw, p, info, s);
   }
   return fail(TK_ERR_UNSUPPORTED, "tk_gemm: no kernel for tile width %d", bn);
+}
+
+// --- GEMM + residual + LayerNorm over rows wider than a tile -----------------
+namespace {
+bool wide_ln_shape(int64_t N) { return N % 256 == 0 && N >= 512 && N <= 4096; }
+int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+}  // namespace
+
+int64_t tk_gemm_resid_ln_workspace_bytes(int64_t M, int64_t N) {
+  if (M <= 0 || !wide_ln_shape(N)) return 0;
+  return align256(M * 4) + align256(M * (N / 128) * 8);  // counters [M] u32, partials [M, N/128] float2
+}
+
+int tk_gemm_resid_ln_supported(int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || K <= 0 || K % 8 != 0) return 0;
+  return (N == 64 || N == 128 || N == 256 || wide_ln_shape(N)) ? 1 : 0;
+}
+
+int tk_gemm_resid_ln(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, const float* resid,
+                     int64_t ld_resid, float* sum_out, int64_t ld_sum, const float* gamma, const float* beta, float eps,
+                     void* out, int out_dtype, int64_t ldo, const int32_t* row_len, int64_t seq_len, int64_t M,
+                     int64_t N, int64_t K, void* workspace, int64_t workspace_bytes, void* stream) {
+  g_last_error.clear();
+  if (N == 64 || N == 128 || N == 256)  // one tile holds the whole row: no workspace
+    return tk_gemm(A, lda, W, ldw, bias, TK_EPI_BIAS_RESID_LN, resid, ld_resid, sum_out, ld_sum, gamma, beta, eps,
+                   out, out_dtype, ldo, row_len, seq_len, M, N, K, stream);
+  if (A == nullptr || W == nullptr || bias == nullptr || resid == nullptr || sum_out == nullptr || gamma == nullptr ||
+      beta == nullptr || out == nullptr)
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: null pointer");
+  if (M < 0 || K <= 0 || M > (1ll << 31) - 1 || K > 65536)
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+                (long long)K);
+  if (!wide_ln_shape(N) || K % 8 != 0)
+    return fail(TK_ERR_UNSUPPORTED, "tk_gemm_resid_ln: needs N in {64,128,256} or N %% 256 == 0 with "
+                "512 <= N <= 4096, and K %% 8 == 0 (N=%lld K=%lld)", (long long)N, (long long)K);
+  if (lda < K || ldw < K || lda % 8 != 0 || ldw % 8 != 0 || !aligned(A, 16) || !aligned(W, 16))
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: A/W need 16-byte aligned rows (ld %% 8 == 0, ld >= K)");
+  if (!aligned(bias, 16) || !aligned(gamma, 16) || !aligned(beta, 16))
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: bias/gamma/beta must be 16-byte aligned");
+  if (ld_resid < N || ld_sum < N || ld_resid % 4 || ld_sum % 4 || !aligned(resid, 16) || !aligned(sum_out, 16))
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: resid/sum_out need 16-byte aligned fp32 rows");
+  if (out_dtype != TK_F16 && out_dtype != TK_F32) return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: out dtype");
+  if (ldo < N || (out_dtype == TK_F32 ? ldo % 4 : ldo % 8) != 0 || !aligned(out, 16))
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: out needs 16-byte aligned rows");
+  if (row_len != nullptr && (seq_len <= 0 || M % seq_len != 0))
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: row_len needs seq_len dividing M");
+  const int64_t need = tk_gemm_resid_ln_workspace_bytes(M, N);
+  if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 256))
+    return fail(TK_ERR_INVALID, "tk_gemm_resid_ln: needs a 256-byte aligned workspace of %lld bytes (got %lld)",
+                (long long)need, (long long)workspace_bytes);
+  if (M == 0) return TK_OK;
+  int dev;
+  DeviceInfo* info;
+  if (int st = current_device(&dev, &info)) return st;
+  CUtensorMap ma, mw;
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(M)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(lda) * 2};
+    cuuint32_t box[2] = {64, 128};
+    if (int st = make_map_f16(&ma, A, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  {
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldw) * 2};
+    cuuint32_t box[2] = {64, 128};
+    if (int st = make_map_f16(&mw, W, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return st;
+  }
+  tk::gemm::Params p;
+  p.M = static_cast<int>(M); p.N = static_cast<int>(N); p.K = static_cast<int>(K);
+  p.bias = bias; p.resid = resid; p.ld_resid = ld_resid; p.sum_out = sum_out; p.ld_sum = ld_sum;
+  p.out = out; p.ldo = ldo; p.out_f32 = out_dtype == TK_F32 ? 1 : 0;
+  p.gamma = gamma; p.beta = beta; p.eps = eps;
+  p.row_len = row_len; p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : 1);
+  p.reduce_add = 0;
+  p.wait_limit_ns = g_wait_limit_ns.load();
+  // Counters at the front, partials at the back: a workspace sized for M
+  // rows serves every M' <= M without the two regions ever overlapping, so
+  // the counters a completed call leaves at zero stay zero.
+  p.ln_parts = static_cast<int>(N / 128);
+  p.ln_count = static_cast<unsigned*>(workspace);
+  p.ln_part = reinterpret_cast<float2*>(static_cast<char*>(workspace) + (workspace_bytes / 256) * 256 -
+                                        align256(M * (N / 128) * 8));
+  return launch_gemm_pair<tk::gemm::kBiasResidLnX>(ma, mw, ma, p, info, static_cast<cudaStream_t>(stream));
 }
 
 int tk_stack_small_supported(int64_t d, int64_t heads, int64_t ffn, int64_t seq_len) {

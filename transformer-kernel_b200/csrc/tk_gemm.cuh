@@ -7,6 +7,10 @@
 //   kBiasGelu     out16 = gelu_erf(acc + b)                    (FFN in, fp32 erf)
 //   kBiasResid    s32   = resid + acc + b                      (O-proj / FFN out)
 //   kBiasResidLn  s32   = resid + acc + b;  h = LN(s) (fp32 statistics), N == BN
+//   kBiasResidLnX s32   = resid + acc + b;  h = LN(s) for rows wider than a tile
+//                 (CTA-pair kernel, N % 256 == 0): per-row partial statistics
+//                 of every 128-column slice go to a workspace, and the last
+//                 warp to publish for a 32-row group normalises those rows
 //
 // A is the fp16 activation [M,K] (row-major = K-major), W the fp16
 // nn.Linear weight [N,K] as-is (also K-major). Both are staged by TMA into
@@ -30,7 +34,7 @@
 namespace tk {
 namespace gemm {
 
-enum Epilogue : int { kBias = 0, kBiasGelu = 1, kBiasResid = 2, kBiasResidLn = 3 };
+enum Epilogue : int { kBias = 0, kBiasGelu = 1, kBiasResid = 2, kBiasResidLn = 3, kBiasResidLnX = 4 };
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;  // one 128-byte swizzle row of fp16
@@ -54,6 +58,9 @@ struct Params {
   int seq_len;             //   (row % seq_len) >= row_len[row / seq_len] are zeroed
   int reduce_add;          // pair kBiasResid: sum_out == resid, no row_len -> TMA reduce-add
   uint64_t wait_limit_ns;
+  float2* ln_part;         // kBiasResidLnX: [M, ln_parts] (mean, centred M2) of each 128-column slice
+  unsigned* ln_count;      //   [M] partials published per row (0 at launch; the last publisher resets it)
+  int ln_parts;            //   N / 128
 };
 
 // Epilogue staging: each epilogue warp transposes 32 rows x 16 fp32 columns
@@ -310,6 +317,231 @@ __device__ __forceinline__ void tma_reduce_epilogue(const Params& p, const CUten
     }
     ++n_stores;
     if (c + 1 < kChunks) tmem_ld_wait(r);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// kBiasResidLnX: residual add + LayerNorm over rows wider than one tile.
+//
+// A pair tile covers 256 of the row's N columns, so no CTA sees a whole row.
+// Each epilogue warp (32 rows x 128 columns) computes s = resid + (acc + b),
+// stores it (the fp32 residual stream, in place), keeps it in TMEM, and takes
+// the row's mean and centred sum of squares over its 128 columns with two
+// passes over TMEM. Each lane publishes its row's (mean, M2) to the workspace
+// and counts it in the row's counter (fence, then atomic add, at GPU scope).
+// The lane whose increment completes a row's count -- all N/128 slices of the
+// row are then in memory -- resets that counter to zero for the next launch,
+// and its warp combines the row's partials exactly (Chan, Golub & LeVeque's
+// pairwise update for equal-size parts: mean = mean of the part means,
+// M2 = sum M2_i + 128 * sum (mean_i - mean)^2), normalises the row over all
+// N columns reading s back from L2 (the other tiles of the row block were
+// written moments before by the neighbouring CTA pairs, the row block's tiles
+// being consecutive in the m-major order) and writes h. On average a warp
+// completes one row in N/128, i.e. 4 of its 32 rows per tile at N = 1024. No warp ever waits for another CTA, so nothing depends on which
+// CTAs are resident at the same time.
+// ----------------------------------------------------------------------------
+
+// TMEM pass of one warp's 32 rows x HALF_N columns. Accumulator chunks go
+// through the swizzled 2 KB stage (thread = row in, lane -> row it*8 + lane/4,
+// float4 column lane%4 out) so that residual loads and sum stores run along
+// rows; s returns through the stage to thread = row, back into TMEM. Returns
+// the thread's row (mean, M2) over its HALF_N columns.
+template <int HALF_N>
+__device__ __forceinline__ float2 resid_stats_epilogue(const Params& p, float* stage, uint32_t t_row, int row_base,
+                                                       int col_base, uint32_t lane) {
+  float4* my_row = reinterpret_cast<float4*>(stage + lane * kStageCols);
+  const uint32_t swz = (lane >> 1) & 3;
+  const int sub_row = static_cast<int>(lane >> 2), sub_c4 = static_cast<int>(lane & 3);
+  constexpr int kChunks = HALF_N / kStageCols;
+  auto load_resid = [&](int c, float4 (&dst)[4]) {
+    const int gcol = col_base + c * kStageCols + sub_c4 * 4;
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int grow = row_base + it * 8 + sub_row;
+      // plain load: resid may alias sum_out (each element is read, then written, by this thread)
+      dst[it] = grow < p.M ? *reinterpret_cast<const float4*>(p.resid + static_cast<int64_t>(grow) * p.ld_resid + gcol)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  bool pad[4];
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int grow = row_base + it * 8 + sub_row;
+    pad[it] = p.row_len != nullptr && grow < p.M && (grow % p.seq_len) >= p.row_len[grow / p.seq_len];
+  }
+  float4 res_cur[4], res_nxt[4];
+  load_resid(0, res_cur);
+  uint32_t r[16];
+  tmem_ld16(t_row, r);
+  tmem_ld_wait(r);
+  float sum = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < kChunks; ++c) {
+    const int col0 = col_base + c * kStageCols;
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4)
+      my_row[j4 ^ swz] = make_float4(__uint_as_float(r[4 * j4 + 0]), __uint_as_float(r[4 * j4 + 1]),
+                                     __uint_as_float(r[4 * j4 + 2]), __uint_as_float(r[4 * j4 + 3]));
+    __syncwarp();
+    if (c + 1 < kChunks) {
+      tmem_ld16(t_row + (c + 1) * kStageCols, r);  // in flight during this chunk
+      load_resid(c + 1, res_nxt);
+    }
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + col0) + sub_c4);
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int rr = it * 8 + sub_row;
+      const int grow = row_base + rr;
+      float4* slot = reinterpret_cast<float4*>(stage + rr * kStageCols) + (sub_c4 ^ ((rr >> 1) & 3));
+      const float4 a = *slot;
+      const float4 rs = res_cur[it];
+      float4 sv = make_float4(rs.x + (a.x + bb.x), rs.y + (a.y + bb.y), rs.z + (a.z + bb.z), rs.w + (a.w + bb.w));
+      if (pad[it]) sv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (grow < p.M)
+        *reinterpret_cast<float4*>(p.sum_out + static_cast<int64_t>(grow) * p.ld_sum + col0 + sub_c4 * 4) = sv;
+      *slot = sv;
+    }
+    __syncwarp();
+    uint32_t sv[16];
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      const float4 v = my_row[j4 ^ swz];
+      sv[4 * j4 + 0] = __float_as_uint(v.x);
+      sv[4 * j4 + 1] = __float_as_uint(v.y);
+      sv[4 * j4 + 2] = __float_as_uint(v.z);
+      sv[4 * j4 + 3] = __float_as_uint(v.w);
+      sum += (v.x + v.y) + (v.z + v.w);
+    }
+    tmem_st16(t_row + c * kStageCols, sv);
+    __syncwarp();  // the next chunk rewrites the stage
+    if (c + 1 < kChunks) {
+      tmem_ld_wait(r);
+#pragma unroll
+      for (int it = 0; it < 4; ++it) res_cur[it] = res_nxt[it];
+    }
+  }
+  tmem_st_wait();
+  const float mean = sum * (1.f / static_cast<float>(HALF_N));
+  float m2 = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < HALF_N; c += 32) {
+    uint32_t q[32];
+    tmem_ld32(t_row + c, q);
+    tmem_ld_wait(q);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float t = __uint_as_float(q[j]) - mean;
+      m2 = fmaf(t, t, m2);
+    }
+  }
+  return make_float2(mean, m2);
+}
+
+// LayerNorm of row `row` over all N columns by the whole warp, from the
+// row's N/128 partials (lane i holds part i; butterfly sums, so every lane
+// computes the same statistics) and s read back from L2; each lane takes the
+// float4 columns lane*4 + 128*i. Two rows per call (rb < 0: one) so that twice
+// the loads are in flight; s loads are issued before the statistics.
+__device__ __forceinline__ void ln_row_stats(const Params& p, int row, uint32_t lane, float& mean, float& rstd) {
+  const int parts = p.ln_parts;
+  const float2 q = static_cast<int>(lane) < parts ? __ldcg(p.ln_part + static_cast<int64_t>(row) * parts + lane)
+                                                  : make_float2(0.f, 0.f);
+  float ms = q.x;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ms += __shfl_xor_sync(0xffffffffu, ms, o);
+  mean = ms / static_cast<float>(parts);
+  const float dm = q.x - mean;
+  float m2 = static_cast<int>(lane) < parts ? q.y + 128.f * dm * dm : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
+  rstd = rsqrtf(m2 * (1.f / static_cast<float>(p.N)) + p.eps);
+}
+
+__device__ __forceinline__ void ln_store4(const Params& p, int row, int c, float4 h) {
+  if (p.out_f32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + c) = h;
+  } else {
+    uint2 o;
+    o.x = pack_half2(h.x, h.y);
+    o.y = pack_half2(h.z, h.w);
+    *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + static_cast<int64_t>(row) * p.ldo + c) = o;
+  }
+}
+
+__device__ __forceinline__ void ln_normalise_rows2(const Params& p, int ra, int rb, uint32_t lane) {
+  const int rows[2] = {ra, rb < 0 ? ra : rb};
+  const int nr = rb < 0 ? 1 : 2;
+  bool pad[2];
+  float mean[2], rstd[2];
+#pragma unroll 1
+  for (int cb = 0; cb < p.N; cb += 1024) {
+    float4 sv[2][8];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float* srow = p.sum_out + static_cast<int64_t>(rows[k]) * p.ld_sum;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c = cb + i * 128 + static_cast<int>(lane) * 4;
+        sv[k][i] = (k < nr && c < p.N) ? __ldcg(reinterpret_cast<const float4*>(srow + c))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    if (cb == 0) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        ln_row_stats(p, rows[k], lane, mean[k], rstd[k]);
+        pad[k] = p.row_len != nullptr && (rows[k] % p.seq_len) >= p.row_len[rows[k] / p.seq_len];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = cb + i * 128 + static_cast<int>(lane) * 4;
+      if (c >= p.N) continue;  // uniform across the warp (N % 256 == 0)
+      const float4 g = __ldg(reinterpret_cast<const float4*>(p.gamma + c));
+      const float4 be = __ldg(reinterpret_cast<const float4*>(p.beta + c));
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        if (k >= nr) continue;
+        const float4 v = sv[k][i];
+        float4 h = make_float4((v.x - mean[k]) * rstd[k] * g.x + be.x, (v.y - mean[k]) * rstd[k] * g.y + be.y,
+                               (v.z - mean[k]) * rstd[k] * g.z + be.z, (v.w - mean[k]) * rstd[k] * g.w + be.w);
+        if (pad[k]) h = make_float4(0.f, 0.f, 0.f, 0.f);
+        ln_store4(p, rows[k], c, h);
+      }
+    }
+  }
+}
+
+// Publish this warp's (mean, M2) partial of each of its 32 rows and count it
+// in the row's counter (one per row). A lane whose increment completes its
+// row's count -- all N/128 partials and slices of s are then in memory --
+// resets the counter to zero (it is the counter's only reader this launch)
+// and the warp normalises every such row, two at a time.
+__device__ __forceinline__ void ln_publish(const Params& p, float2 st, int row_base, int part, uint32_t lane) {
+  const int row = row_base + static_cast<int>(lane);
+  bool last = false;
+  if (row < p.M) p.ln_part[static_cast<int64_t>(row) * p.ln_parts + part] = st;
+  __threadfence();  // every lane's stores of s and of its partial, at GPU scope,
+  __syncwarp();     // before any lane of the warp counts its row
+  if (row < p.M) {
+    const unsigned old = atomicAdd(p.ln_count + row, 1u);
+    last = old + 1u == static_cast<unsigned>(p.ln_parts);
+    if (last) {
+      p.ln_count[row] = 0u;
+      __threadfence();  // the other publishers' data after their counts
+    }
+  }
+  unsigned mask = __ballot_sync(0xffffffffu, last);
+  __syncwarp();
+  while (mask != 0u) {
+    const int a = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    int b = -1;
+    if (mask != 0u) {
+      b = __ffs(mask) - 1;
+      mask &= mask - 1u;
+    }
+    ln_normalise_rows2(p, row_base + a, b < 0 ? -1 : row_base + b, lane);
   }
 }
 
@@ -652,7 +884,7 @@ template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                      const __grid_constant__ CUtensorMap map_out, Params p) {
-  static_assert(EPI != kBiasResidLn, "pair kernel has no LayerNorm epilogue");
+  static_assert(EPI != kBiasResidLn, "the pair kernel's LayerNorm epilogue is kBiasResidLnX");
   using C = PairCfg;
   constexpr int TN = 256;  // pair tile: 256 rows x 256 columns
   extern __shared__ uint8_t smem_raw[];
@@ -801,7 +1033,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if constexpr (EPI == kBiasResid) {
+      if constexpr (EPI == kBiasResid || EPI == kBiasResidLnX) {
         // The residual rows of this warp's slice of the next tile go to L2
         // now, a whole main loop ahead of their use.
         const int next = tile + npairs;
@@ -820,18 +1052,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int m0 = (tile / n_tiles) * 2 * kBM + static_cast<int>(rank) * kBM;
       const int n0 = (tile % n_tiles) * TN;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * TN + half * HALF_N;
+      float2 ln_st = make_float2(0.f, 0.f);
       if constexpr (EPI == kBiasResid) {
         if (p.reduce_add)
           tma_reduce_epilogue<HALF_N>(p, &map_out, stage, t_row, m0 + quad * 32, n0 + half * HALF_N, lane, n_stores);
         else
           staged_epilogue<HALF_N, EPI>(p, reinterpret_cast<float*>(stage), t_row, m0 + quad * 32,
                                        n0 + half * HALF_N, lane);
+      } else if constexpr (EPI == kBiasResidLnX) {
+        ln_st = resid_stats_epilogue<HALF_N>(p, reinterpret_cast<float*>(stage), t_row, m0 + quad * 32,
+                                             n0 + half * HALF_N, lane);
       } else
         tma_store_epilogue<HALF_N, EPI>(p, &map_out, stage, t_row, m0 + quad * 32, n0 + half * HALF_N, lane,
                                         n_stores);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+      // TMEM is released first: the next tile's main loop may proceed while
+      // this warp publishes its statistics (and, when last, normalises rows).
+      if constexpr (EPI == kBiasResidLnX) ln_publish(p, ln_st, m0 + quad * 32, (n0 + half * HALF_N) / 128, lane);
+      (void)ln_st;
     }
     if (lane == 0) bulk_wait_all();  // stores complete before the CTA's shared memory goes away
   }

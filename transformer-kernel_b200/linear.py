@@ -9,7 +9,10 @@ fuses what follows the projection in the reference's forward
 * ``"gelu"``          -> fp16 ``gelu_erf(a @ w.T + b)`` (fp32 erf)
 * ``"resid"``         -> fp32 ``s = resid + a @ w.T + b`` (written to ``sum_out``)
 * ``"resid_ln"``      -> as ``"resid"``, and ``out = LayerNorm(s)`` with fp32
-  statistics, for ``N`` in {64, 128, 256}
+  statistics: ``N`` in {64, 128, 256} in one tile (``tk_gemm``), or
+  ``N % 256 == 0`` up to 4096 with per-row partial statistics in a workspace
+  (``tk_gemm_resid_ln``; pass ``workspace``, a zeroed uint8 tensor of
+  ``ln_workspace_bytes(M, N)`` bytes, to reuse one across calls)
 
 ``w`` is the ``nn.Linear`` weight ``[N, K]`` in fp16 as-is. No fallback.
 """
@@ -31,7 +34,14 @@ EPILOGUES = {
 
 
 def fused_ln_supported(n: int) -> bool:
-    return n in (64, 128, 256)
+    """Whether residual add + LayerNorm fuses into the GEMM for rows of n."""
+    return bool(tk.lib().tk_gemm_resid_ln_supported(1, int(n), 8))
+
+
+def ln_workspace_bytes(m: int, n: int) -> int:
+    """Workspace bytes of a ``"resid_ln"`` GEMM with m rows of n columns (0
+    when one tile holds the row)."""
+    return int(tk.lib().tk_gemm_resid_ln_workspace_bytes(int(m), int(n)))
 
 
 def linear(
@@ -49,6 +59,7 @@ def linear(
     out_dtype: torch.dtype = torch.float16,
     row_len: Optional[torch.Tensor] = None,
     seq_len: int = 0,
+    workspace: Optional[torch.Tensor] = None,
 ):
     """Run one fused GEMM on 2-D row-major operands. Returns ``out`` for
     ``bias``/``gelu``, ``sum_out`` for ``resid`` and ``(sum_out, out)`` for
@@ -77,6 +88,23 @@ def linear(
     beta = None if ln_bias is None else ln_bias.float().contiguous()
     if row_len is not None:
         row_len = row_len.to(torch.int32).contiguous()
+    if epi == tk.EPI_BIAS_RESID_LN and N not in (64, 128, 256):
+        need = ln_workspace_bytes(M, N)
+        if workspace is None:
+            workspace = torch.zeros(need, dtype=torch.uint8, device=dev)
+        if workspace.dtype != torch.uint8 or workspace.numel() < need or not workspace.is_contiguous():
+            raise ValueError(f"workspace must be a contiguous uint8 tensor of >= {need} bytes")
+        with torch.cuda.device(dev):
+            tk.call(
+                "tk_gemm_resid_ln",
+                a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), bias.data_ptr(),
+                resid.data_ptr(), resid.stride(0), sum_out.data_ptr(), sum_out.stride(0),
+                gamma.data_ptr(), beta.data_ptr(), float(eps),
+                out.data_ptr(), tk.dtype_code(out.dtype), out.stride(0),
+                tk.ptr(row_len), int(seq_len), M, N, K,
+                workspace.data_ptr(), workspace.numel(), tk.stream_handle(dev),
+            )
+        return sum_out, out
     with torch.cuda.device(dev):
         tk.call(
             "tk_gemm",

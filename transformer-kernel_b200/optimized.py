@@ -17,13 +17,14 @@ reference does (:224-244).
 
 Forward, per layer (``T = B*S`` token rows, fp32 residual stream):
 
-  h    = LN1(x)                                   tk_layernorm        (layer 0 only)
+  h, x = LN1(x), copy of x                        tk_layernorm        (layer 0 only)
   qkv  = h Wqkv^T + bqkv                          tk_gemm  BIAS       fp16 [T, 3d]
   ctx  = attention(q, k, v views of qkv)          tk_attn_fwd         fp16 [T, d]
-  x, h = x + ctx Wo^T + bo,  LN2(.)               tk_gemm  RESID_LN   (d in {64,128,256})
-                                                  or RESID + tk_layernorm
+  x, h = x + ctx Wo^T + bo,  LN2(.)               tk_gemm_resid_ln    (d in {64,128,256} or
+                                                  d % 256 == 0 up to 4096), else
+                                                  tk_gemm RESID + tk_layernorm
   u    = gelu(h W1^T + b1)                        tk_gemm  GELU       fp16 [T, ffn]
-  x, h = x + u W2^T + b2,  next LN1 / final LN    tk_gemm  RESID_LN  or RESID + tk_layernorm
+  x, h = x + u W2^T + b2,  next LN1 / final LN    as the O-projection
 
 The final LayerNorm writes the fp32 output directly. There is no CPU,
 SDPA, cuBLAS or Triton path: anything the kernels cannot do raises.
@@ -65,8 +66,10 @@ class OptimizerSettings:
     """Knobs of the B200 forward. None of them selects another backend."""
 
     # Fuse residual add + LayerNorm into the O-projection / FFN-out GEMM
-    # epilogue when d_model fits one tile row (64, 128 or 256); wider models
-    # use the GEMM residual epilogue followed by tk_layernorm.
+    # epilogue: in one tile when d_model is 64, 128 or 256, through per-row
+    # partial statistics across the CTA-pair tiles when d_model % 256 == 0
+    # (up to 4096); other widths use the GEMM residual epilogue followed by
+    # tk_layernorm.
     fused_ln_epilogue: bool = True
     # Skip the one device->host sync that checks whether the mask is all-True.
     assume_dense_mask: bool = False
@@ -285,15 +288,19 @@ class OptimizedTransformer(nn.Module):
 
     def _activations(self, B: int, S: int, d: int, ffn: int, dev: torch.device):
         """Activation buffers of one forward: residual stream fp32 [T, d], h
-        fp16 [T, d], qkv fp16 [T, 3d], ctx fp16 [B, S, d], u fp16 [T, ffn] and
-        the output fp32 [T, d], from the caching allocator."""
+        fp16 [T, d], qkv fp16 [T, 3d], ctx fp16 [B, S, d], u fp16 [T, ffn],
+        the output fp32 [T, d], and the (zeroed) workspace of the residual +
+        LayerNorm GEMMs for rows wider than a tile, from the caching
+        allocator. A workspace sized for T rows serves any shorter forward."""
         T = B * S
+        ws = max(256, tk_linear.ln_workspace_bytes(T, d))
         return (torch.empty((T, d), dtype=torch.float32, device=dev),
                 torch.empty((T, d), dtype=torch.float16, device=dev),
                 torch.empty((T, 3 * d), dtype=torch.float16, device=dev),
                 torch.empty((B, S, d), dtype=torch.float16, device=dev),
                 torch.empty((T, ffn), dtype=torch.float16, device=dev),
-                torch.empty((T, d), dtype=torch.float32, device=dev))
+                torch.empty((T, d), dtype=torch.float32, device=dev),
+                torch.zeros(ws, dtype=torch.uint8, device=dev))
 
     def _uses_small_stack(self, x: torch.Tensor) -> bool:
         """Whether a forward over x runs as one tk_stack_small launch."""
@@ -366,7 +373,7 @@ class OptimizedTransformer(nn.Module):
         """Every launch after ``_head``: the layers (the residual stream is
         updated in place) and the final LayerNorm into ``out`` (default the
         forward's own output buffer). Returns the output as [B, S, d]."""
-        res, h, qkv, ctx, u, out_ws = bufs
+        res, h, qkv, ctx, u, out_ws, ln_ws = bufs
         T, d = res.shape
         ffn = u.shape[1]
         hd = self.head_dim
@@ -385,7 +392,7 @@ class OptimizedTransformer(nn.Module):
             ctx2 = ctx.view(T, d)
             if fused:
                 run("gemm_o_ln", lin, ctx2, w.out_w, w.out_b, "resid_ln", resid=res, sum_out=res,
-                    ln_weight=w.norm2_w, ln_bias=w.norm2_b, eps=w.norm2_eps, out=h)
+                    ln_weight=w.norm2_w, ln_bias=w.norm2_b, eps=w.norm2_eps, out=h, workspace=ln_ws)
             else:
                 run("gemm_o", lin, ctx2, w.out_w, w.out_b, "resid", resid=res, sum_out=res)
                 run("ln", self._layer_norm, res, w.norm2_w, w.norm2_b, w.norm2_eps, h)
@@ -397,7 +404,7 @@ class OptimizedTransformer(nn.Module):
                 dst = out
             if fused:
                 run("gemm_ffn_out_ln", lin, u, w.ffn_out_w, w.ffn_out_b, "resid_ln", resid=res, sum_out=res,
-                    ln_weight=nw, ln_bias=nb, eps=neps, out=dst, row_len=lengths, seq_len=seq)
+                    ln_weight=nw, ln_bias=nb, eps=neps, out=dst, row_len=lengths, seq_len=seq, workspace=ln_ws)
             else:
                 run("gemm_ffn_out", lin, u, w.ffn_out_w, w.ffn_out_b, "resid", resid=res, sum_out=res,
                     row_len=lengths, seq_len=seq)
@@ -533,7 +540,9 @@ class OptimizedTransformer(nn.Module):
         if lengths is not None or self._uses_small_stack(xs):
             self._run(xs, lengths, out=os_)
             return
-        bufs = tuple(b[:nb * S] if b.dim() == 2 else b[:nb] for b in slot["bufs"])
+        # views of the slot's buffers for nb sequences; the workspace (last)
+        # serves any row count up to the one it was sized for
+        bufs = tuple(b[:nb * S] if b.dim() == 2 else b[:nb] for b in slot["bufs"][:-1]) + (slot["bufs"][-1],)
         g = slot["graphs"].get(nb)
         if g is None:
             self._head(xs, bufs, weights)
