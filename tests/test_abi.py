@@ -101,9 +101,9 @@ def test_resid_ln_workspace_and_support_on_host():
     lib = tk.lib()
     # one tile holds rows of 64/128/256: no workspace
     assert lib.tk_gemm_resid_ln_workspace_bytes(65536, 256) == 0
-    # counters [M] u32 + partials [M, N/128] float2, each 256-byte aligned
-    assert lib.tk_gemm_resid_ln_workspace_bytes(65536, 1024) == 65536 * 4 + 65536 * 8 * 8
-    assert lib.tk_gemm_resid_ln_workspace_bytes(1000, 512) == 4096 + 32000
+    # state words [M] u64 + partials [M, N/128] float2, each 256-byte aligned
+    assert lib.tk_gemm_resid_ln_workspace_bytes(65536, 1024) == 65536 * 8 + 65536 * 8 * 8
+    assert lib.tk_gemm_resid_ln_workspace_bytes(1000, 512) == 8192 + 32000
     assert lib.tk_gemm_resid_ln_supported(65536, 1024, 4096) == 1
     assert lib.tk_gemm_resid_ln_supported(65536, 640, 4096) == 0   # not a multiple of 256
     assert lib.tk_gemm_resid_ln_supported(65536, 8192, 4096) == 0  # above 4096

@@ -278,8 +278,8 @@ def test_gemm_resid_ln_in_place_workspace_reuse(cuda_device):
         torch.testing.assert_close(res.cpu(), want_s, atol=1e-4, rtol=1e-4)
         torch.testing.assert_close(h.float().cpu(), F.layer_norm(want_s, (N,), g, beta, 1e-5), atol=2e-3, rtol=2e-2)
     torch.cuda.synchronize()
-    count_bytes = (Mbig * 4 + 255) // 256 * 256
-    assert int(ws[:count_bytes].view(torch.int32).abs().sum()) == 0  # every row counter back at zero
+    count_bytes = (Mbig * 8 + 255) // 256 * 256
+    assert int(ws[:count_bytes].view(torch.int64).abs().sum()) == 0  # every row state word back at zero
 
 
 def test_gemm_resid_ln_row_len_and_large_mean(cuda_device):

@@ -98,6 +98,23 @@ def test_fused_and_unfused_layernorm_paths_agree(cuda_device):
     torch.testing.assert_close(a, b, atol=1e-3, rtol=0)
 
 
+@pytest.mark.parametrize("cfg", [StackConfig(4, 256, 1024, 16, 4096, 4, False), StackConfig(1, 512, 512, 8, 2048, 4, True),
+                                 StackConfig(3, 200, 768, 12, 1024, 2, True)], ids=["d1024", "d512", "d768"])
+def test_wide_fused_layernorm_stack(cuda_device, cfg):
+    """The forward with residual + LayerNorm fused across CTA-pair tiles
+    (tk_gemm_resid_ln) against the oracle, padded rows included, and against
+    the default GEMM-then-LayerNorm path."""
+    check(cfg, seeds=[1234], fused_wide_ln=True)
+    check(cfg, seeds=[1235], padding_ratio=0.3, fused_wide_ln=True)
+    _, fused = build(cfg, fused_wide_ln=True)
+    _, plain = build(cfg)
+    x, mask = generate_random_case(cfg, 98)
+    with torch.inference_mode():
+        a = fused(x.cuda(), mask.cuda())
+        b = plain(x.cuda(), mask.cuda())
+    torch.testing.assert_close(a, b, atol=2e-3, rtol=2e-2)
+
+
 def test_state_dict_keys_match_harness(cuda_device, golden):
     cfg = StackConfig(**golden["c1_reference_case1"]["config"])
     model = optimized.OptimizedTransformer(cfg)

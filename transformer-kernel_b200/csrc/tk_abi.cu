@@ -434,7 +434,7 @@ int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
 int64_t tk_gemm_resid_ln_workspace_bytes(int64_t M, int64_t N) {
   if (M <= 0 || !wide_ln_shape(N)) return 0;
-  return align256(M * 4) + align256(M * (N / 128) * 8);  // counters [M] u32, partials [M, N/128] float2
+  return align256(M * 8) + align256(M * (N / 128) * 8);  // state words [M] u64, partials [M, N/128] float2
 }
 
 int tk_gemm_resid_ln_supported(int64_t M, int64_t N, int64_t K) {
@@ -499,11 +499,11 @@ int tk_gemm_resid_ln(const void* A, int64_t lda, const void* W, int64_t ldw, con
   p.row_len = row_len; p.seq_len = static_cast<int>(seq_len > 0 ? seq_len : 1);
   p.reduce_add = 0;
   p.wait_limit_ns = g_wait_limit_ns.load();
-  // Counters at the front, partials at the back: a workspace sized for M
+  // State words at the front, partials at the back: a workspace sized for M
   // rows serves every M' <= M without the two regions ever overlapping, so
-  // the counters a completed call leaves at zero stay zero.
+  // the words a completed call leaves at zero stay zero.
   p.ln_parts = static_cast<int>(N / 128);
-  p.ln_count = static_cast<unsigned*>(workspace);
+  p.ln_state = static_cast<unsigned long long*>(workspace);
   p.ln_part = reinterpret_cast<float2*>(static_cast<char*>(workspace) + (workspace_bytes / 256) * 256 -
                                         align256(M * (N / 128) * 8));
   return launch_gemm_pair<tk::gemm::kBiasResidLnX>(ma, mw, ma, p, info, static_cast<cudaStream_t>(stream));

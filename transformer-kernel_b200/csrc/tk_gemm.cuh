@@ -59,7 +59,7 @@ struct Params {
   int reduce_add;          // pair kBiasResid: sum_out == resid, no row_len -> TMA reduce-add
   uint64_t wait_limit_ns;
   float2* ln_part;         // kBiasResidLnX: [M, ln_parts] (mean, centred M2) of each 128-column slice
-  unsigned* ln_count;      //   [M] partials published per row (0 at launch; the last publisher resets it)
+  unsigned long long* ln_state;  //   [M] per-row state word (0 at launch; zero again when the row is done)
   int ln_parts;            //   N / 128
 };
 
@@ -324,21 +324,27 @@ __device__ __forceinline__ void tma_reduce_epilogue(const Params& p, const CUten
 // kBiasResidLnX: residual add + LayerNorm over rows wider than one tile.
 //
 // A pair tile covers 256 of the row's N columns, so no CTA sees a whole row.
-// Each epilogue warp (32 rows x 128 columns) computes s = resid + (acc + b),
-// stores it (the fp32 residual stream, in place), keeps it in TMEM, and takes
-// the row's mean and centred sum of squares over its 128 columns with two
-// passes over TMEM. Each lane publishes its row's (mean, M2) to the workspace
-// and counts it in the row's counter (fence, then atomic add, at GPU scope).
-// The lane whose increment completes a row's count -- all N/128 slices of the
-// row are then in memory -- resets that counter to zero for the next launch,
-// and its warp combines the row's partials exactly (Chan, Golub & LeVeque's
-// pairwise update for equal-size parts: mean = mean of the part means,
-// M2 = sum M2_i + 128 * sum (mean_i - mean)^2), normalises the row over all
-// N columns reading s back from L2 (the other tiles of the row block were
-// written moments before by the neighbouring CTA pairs, the row block's tiles
-// being consecutive in the m-major order) and writes h. On average a warp
-// completes one row in N/128, i.e. 4 of its 32 rows per tile at N = 1024. No warp ever waits for another CTA, so nothing depends on which
-// CTAs are resident at the same time.
+// Each epilogue warp (32 rows x one 128-column slice) computes
+// s = resid + (acc + b), stores it (the fp32 residual stream, in place),
+// keeps it in TMEM, and takes each row's mean and centred sum of squares over
+// its slice with two passes over TMEM. It publishes the (mean, M2) partials
+// to the workspace and counts them in the rows' state words (fence, then
+// atomic add, at GPU scope), and releases its TMEM accumulator.
+//
+// The warp keeps the slice pending and, after each later tile, checks the
+// rows' words: once the other slices of those rows (computed by the
+// neighbouring CTA pairs in the same wave) are all published, it normalises
+// its own slice of the 32 rows: it combines the row's N/128 partials exactly
+// (Chan, Golub & LeVeque's update for equal-size parts: mean = mean of the
+// part means, M2 = sum M2_i + 128 * sum (mean_i - mean)^2), reads its slice
+// of s back from L2 and writes h. Every warp normalises exactly the slices it
+// computed, so a CTA pair running late never inherits extra work. Only when
+// a slice cannot stay pending (more than two pending, or the warp's last
+// tile is done) and its rows are still incomplete is it handed to the rows'
+// last publisher through the state word. No warp ever waits for another
+// CTA, so nothing depends on which CTAs are resident at the same time. The
+// last slice of a row to be normalised zeroes the row's word for the next
+// launch.
 // ----------------------------------------------------------------------------
 
 // TMEM pass of one warp's 32 rows x HALF_N columns. Accumulator chunks go
@@ -437,27 +443,85 @@ __device__ __forceinline__ float2 resid_stats_epilogue(const Params& p, float* s
   return make_float2(mean, m2);
 }
 
-// LayerNorm of row `row` over all N columns by the whole warp, from the
-// row's N/128 partials (lane i holds part i; butterfly sums, so every lane
-// computes the same statistics) and s read back from L2; each lane takes the
-// float4 columns lane*4 + 128*i. Two rows per call (rb < 0: one) so that twice
-// the loads are in flight; s loads are issued before the statistics.
-__device__ __forceinline__ void ln_row_stats(const Params& p, int row, uint32_t lane, float& mean, float& rstd) {
-  const int parts = p.ln_parts;
-  const float2 q = static_cast<int>(lane) < parts ? __ldcg(p.ln_part + static_cast<int64_t>(row) * parts + lane)
-                                                  : make_float2(0.f, 0.f);
-  float ms = q.x;
+// Per-row state word (u64) of kBiasResidLnX: bits 0-7 count published
+// partials, bits 8-15 count normalised 128-column slices, bit 32+k marks
+// slice k as handed to the last publisher. Every access is an atomic on the
+// word, so the order of any two accesses is total.
+constexpr unsigned long long kLnPub = 1ull, kLnDone = 1ull << 8;
+__device__ __forceinline__ unsigned ln_published(unsigned long long w) { return static_cast<unsigned>(w & 0xFFu); }
+__device__ __forceinline__ unsigned ln_normalised(unsigned long long w) {
+  return static_cast<unsigned>((w >> 8) & 0xFFu);
+}
+
+// Row statistics from the row's N/128 partials, combined in a fixed order by
+// one thread, so every slice of a row is normalised with the same bits. Up
+// to eight partials (N <= 1024) are fetched with four independent 16-byte
+// loads and combined in registers; wider rows read them twice (means, then
+// the centred terms), eight at a time.
+__device__ __forceinline__ void ln_row_stats(const Params& p, int row, float& mean, float& rstd) {
+  const float4* q = reinterpret_cast<const float4*>(p.ln_part + static_cast<int64_t>(row) * p.ln_parts);
+  const int parts = p.ln_parts;  // even (N % 256 == 0)
+  float m2 = 0.f;
+  if (parts <= 8) {
+    float2 v[8];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ms += __shfl_xor_sync(0xffffffffu, ms, o);
-  mean = ms / static_cast<float>(parts);
-  const float dm = q.x - mean;
-  float m2 = static_cast<int>(lane) < parts ? q.y + 128.f * dm * dm : 0.f;
+    for (int i = 0; i < 4; ++i) {
+      const float4 t = 2 * i < parts ? __ldcg(q + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[2 * i] = make_float2(t.x, t.y);
+      v[2 * i + 1] = make_float2(t.z, t.w);
+    }
+    float ms = 0.f;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, o);
+    for (int i = 0; i < 8; ++i)
+      if (i < parts) ms += v[i].x;
+    mean = ms / static_cast<float>(parts);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i < parts) {
+        const float dm = v[i].x - mean;
+        m2 += v[i].y + 128.f * dm * dm;
+      }
+    }
+  } else {
+    float ms = 0.f;
+#pragma unroll 1
+    for (int i0 = 0; i0 < parts / 2; i0 += 4) {
+      float4 t[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) t[i] = i0 + i < parts / 2 ? __ldcg(q + i0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ms += t[i].x + t[i].z;
+    }
+    mean = ms / static_cast<float>(parts);
+#pragma unroll 1
+    for (int i0 = 0; i0 < parts / 2; i0 += 4) {
+      float4 t[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) t[i] = i0 + i < parts / 2 ? __ldcg(q + i0 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (i0 + i < parts / 2) {
+          const float d0 = t[i].x - mean, d1 = t[i].z - mean;
+          m2 += t[i].y + 128.f * d0 * d0;
+          m2 += t[i].w + 128.f * d1 * d1;
+        }
+      }
+    }
+  }
   rstd = rsqrtf(m2 * (1.f / static_cast<float>(p.N)) + p.eps);
 }
 
-__device__ __forceinline__ void ln_store4(const Params& p, int row, int c, float4 h) {
+// h = LN(s) on columns [slice*128, slice*128 + 128) of one row, by the warp
+// (lane -> float4 column lane*4; one coalesced 512-byte row segment).
+__device__ __forceinline__ void ln_slice_row(const Params& p, int row, int slice, float mean, float rstd, bool pad,
+                                             uint32_t lane) {
+  const int c = slice * 128 + static_cast<int>(lane) * 4;
+  const float4 v = __ldcg(reinterpret_cast<const float4*>(p.sum_out + static_cast<int64_t>(row) * p.ld_sum + c));
+  const float4 g = __ldg(reinterpret_cast<const float4*>(p.gamma + c));
+  const float4 be = __ldg(reinterpret_cast<const float4*>(p.beta + c));
+  float4 h = make_float4((v.x - mean) * rstd * g.x + be.x, (v.y - mean) * rstd * g.y + be.y,
+                         (v.z - mean) * rstd * g.z + be.z, (v.w - mean) * rstd * g.w + be.w);
+  if (pad) h = make_float4(0.f, 0.f, 0.f, 0.f);
   if (p.out_f32) {
     *reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(row) * p.ldo + c) = h;
   } else {
@@ -468,81 +532,144 @@ __device__ __forceinline__ void ln_store4(const Params& p, int row, int c, float
   }
 }
 
-__device__ __forceinline__ void ln_normalise_rows2(const Params& p, int ra, int rb, uint32_t lane) {
-  const int rows[2] = {ra, rb < 0 ? ra : rb};
-  const int nr = rb < 0 ? 1 : 2;
-  bool pad[2];
-  float mean[2], rstd[2];
-#pragma unroll 1
-  for (int cb = 0; cb < p.N; cb += 1024) {
-    float4 sv[2][8];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const float* srow = p.sum_out + static_cast<int64_t>(rows[k]) * p.ld_sum;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int c = cb + i * 128 + static_cast<int>(lane) * 4;
-        sv[k][i] = (k < nr && c < p.N) ? __ldcg(reinterpret_cast<const float4*>(srow + c))
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+// Count `n` normalised slices of `row`; the count that completes the row
+// zeroes its word for the next launch (every other access to the word in
+// this launch precedes it: a slice is normalised only after its owner's
+// check and after the row's last publication).
+__device__ __forceinline__ void ln_count_done(const Params& p, int row, unsigned n) {
+  unsigned long long* w = p.ln_state + row;
+  const unsigned long long old = atomicAdd(w, kLnDone * n);
+  if (ln_normalised(old) + n == static_cast<unsigned>(p.ln_parts)) atomicExch(w, 0ull);
+}
+
+__device__ __forceinline__ bool ln_row_pad(const Params& p, int row) {
+  return p.row_len != nullptr && (row % p.seq_len) >= p.row_len[row / p.seq_len];
+}
+
+// Publish this warp's (mean, M2) partial of each of its 32 rows. A lane whose
+// publication completes its row takes over the slices of that row whose
+// owners found it incomplete (rare: the row block straddled a wave), and the
+// warp normalises them.
+__device__ __forceinline__ void ln_publish(const Params& p, float2 st, int row_base, int part, uint32_t lane) {
+  const int row = row_base + static_cast<int>(lane);
+  if (row < p.M) p.ln_part[static_cast<int64_t>(row) * p.ln_parts + part] = st;
+  __threadfence();  // every lane's stores of s and of its partial, at GPU scope,
+  __syncwarp();     // before any lane of the warp publishes
+  unsigned orphans = 0;
+  if (row < p.M) {
+    const unsigned long long old = atomicAdd(p.ln_state + row, kLnPub);
+    if (ln_published(old) + 1u == static_cast<unsigned>(p.ln_parts)) orphans = static_cast<unsigned>(old >> 32);
+  }
+  unsigned mask = __ballot_sync(0xffffffffu, orphans != 0u);
+  if (mask == 0u) return;
+  __threadfence();  // the other publishers' data after their publications
+  float mean = 0.f, rstd = 0.f;
+  if (orphans != 0u) ln_row_stats(p, row, mean, rstd);
+  const bool pad = row < p.M && ln_row_pad(p, row);
+  while (mask != 0u) {
+    const int r = __ffs(mask) - 1;
+    mask &= mask - 1u;
+    unsigned bits = __shfl_sync(0xffffffffu, orphans, r);
+    const float m = __shfl_sync(0xffffffffu, mean, r), rs = __shfl_sync(0xffffffffu, rstd, r);
+    const bool pd = __shfl_sync(0xffffffffu, pad, r);
+    const unsigned n = __popc(bits);
+    while (bits != 0u) {
+      const int k = __ffs(bits) - 1;
+      bits &= bits - 1u;
+      ln_slice_row(p, row_base + r, k, m, rs, pd, lane);
     }
-    if (cb == 0) {
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        ln_row_stats(p, rows[k], lane, mean[k], rstd[k]);
-        pad[k] = p.row_len != nullptr && (rows[k] % p.seq_len) >= p.row_len[rows[k] / p.seq_len];
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int c = cb + i * 128 + static_cast<int>(lane) * 4;
-      if (c >= p.N) continue;  // uniform across the warp (N % 256 == 0)
-      const float4 g = __ldg(reinterpret_cast<const float4*>(p.gamma + c));
-      const float4 be = __ldg(reinterpret_cast<const float4*>(p.beta + c));
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        if (k >= nr) continue;
-        const float4 v = sv[k][i];
-        float4 h = make_float4((v.x - mean[k]) * rstd[k] * g.x + be.x, (v.y - mean[k]) * rstd[k] * g.y + be.y,
-                               (v.z - mean[k]) * rstd[k] * g.z + be.z, (v.w - mean[k]) * rstd[k] * g.w + be.w);
-        if (pad[k]) h = make_float4(0.f, 0.f, 0.f, 0.f);
-        ln_store4(p, rows[k], c, h);
-      }
-    }
+    if (static_cast<int>(lane) == r) ln_count_done(p, row, n);
   }
 }
 
-// Publish this warp's (mean, M2) partial of each of its 32 rows and count it
-// in the row's counter (one per row). A lane whose increment completes its
-// row's count -- all N/128 partials and slices of s are then in memory --
-// resets the counter to zero (it is the counter's only reader this launch)
-// and the warp normalises every such row, two at a time.
-__device__ __forceinline__ void ln_publish(const Params& p, float2 st, int row_base, int part, uint32_t lane) {
+// The owner's normalisation of its own slice of 32 rows (lane -> float4
+// column lane*4, a 512-byte coalesced segment per row; four batches of eight
+// rows, each batch's loads issued while the previous one is normalised).
+// `rows` is the mask of rows to normalise (complete ones).
+__device__ __forceinline__ void ln_slice_rows(const Params& p, int row_base, int part, unsigned rows, bool mine,
+                                              uint32_t lane) {
   const int row = row_base + static_cast<int>(lane);
-  bool last = false;
-  if (row < p.M) p.ln_part[static_cast<int64_t>(row) * p.ln_parts + part] = st;
-  __threadfence();  // every lane's stores of s and of its partial, at GPU scope,
-  __syncwarp();     // before any lane of the warp counts its row
+  const int c = part * 128 + static_cast<int>(lane) * 4;
+  auto load_batch = [&](int b, float4 (&dst)[8]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int r = row_base + b * 8 + j;
+      dst[j] = ((rows >> (b * 8 + j)) & 1u)
+                   ? __ldcg(reinterpret_cast<const float4*>(p.sum_out + static_cast<int64_t>(r) * p.ld_sum + c))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  float4 cur[8], nxt[8];
+  load_batch(0, cur);
+  float mean = 0.f, rstd = 0.f;
+  if (mine) ln_row_stats(p, row, mean, rstd);
+  const bool pad = mine && ln_row_pad(p, row);
+  const float4 g = __ldg(reinterpret_cast<const float4*>(p.gamma + c));
+  const float4 be = __ldg(reinterpret_cast<const float4*>(p.beta + c));
+#pragma unroll 1
+  for (int b = 0; b < 4; ++b) {
+    if ((rows >> (b * 8)) == 0u) break;  // no rows left
+    if (b + 1 < 4) load_batch(b + 1, nxt);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int rr = b * 8 + j;
+      const float m = __shfl_sync(0xffffffffu, mean, rr), rs = __shfl_sync(0xffffffffu, rstd, rr);
+      const bool pd = __shfl_sync(0xffffffffu, pad, rr);
+      if (!((rows >> rr) & 1u)) continue;
+      const float4 v = cur[j];
+      float4 h = make_float4((v.x - m) * rs * g.x + be.x, (v.y - m) * rs * g.y + be.y, (v.z - m) * rs * g.z + be.z,
+                             (v.w - m) * rs * g.w + be.w);
+      if (pd) h = make_float4(0.f, 0.f, 0.f, 0.f);
+      const int r = row_base + rr;
+      if (p.out_f32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + static_cast<int64_t>(r) * p.ldo + c) = h;
+      } else {
+        uint2 o;
+        o.x = pack_half2(h.x, h.y);
+        o.y = pack_half2(h.z, h.w);
+        *reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + static_cast<int64_t>(r) * p.ldo + c) = o;
+      }
+    }
+    if (b + 1 < 4) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+    }
+  }
+  if (mine) ln_count_done(p, row, 1u);
+}
+
+// Try to normalise a pending slice: if every published row of it is complete
+// (a plain acquire read of the row words; the rows of a slice complete
+// together, when the last of their N/128 publishers counts them), normalise
+// it and return true; otherwise leave it pending.
+__device__ __forceinline__ bool ln_try_slice(const Params& p, int row_base, int part, uint32_t lane) {
+  const int row = row_base + static_cast<int>(lane);
+  bool done = true;
   if (row < p.M) {
-    const unsigned old = atomicAdd(p.ln_count + row, 1u);
-    last = old + 1u == static_cast<unsigned>(p.ln_parts);
-    if (last) {
-      p.ln_count[row] = 0u;
-      __threadfence();  // the other publishers' data after their counts
-    }
+    unsigned long long w;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p.ln_state + row) : "memory");
+    done = ln_published(w) == static_cast<unsigned>(p.ln_parts);
   }
-  unsigned mask = __ballot_sync(0xffffffffu, last);
-  __syncwarp();
-  while (mask != 0u) {
-    const int a = __ffs(mask) - 1;
-    mask &= mask - 1u;
-    int b = -1;
-    if (mask != 0u) {
-      b = __ffs(mask) - 1;
-      mask &= mask - 1u;
-    }
-    ln_normalise_rows2(p, row_base + a, b < 0 ? -1 : row_base + b, lane);
+  if (!__all_sync(0xffffffffu, done)) return false;
+  ln_slice_rows(p, row_base, part, __ballot_sync(0xffffffffu, row < p.M), row < p.M, lane);
+  return true;
+}
+
+// A slice that cannot stay pending any longer: rows complete now are
+// normalised here; the others are handed to their last publisher (the
+// atomic OR orders the two: either the owner sees the count complete, or the
+// last publisher sees the mark).
+__device__ __forceinline__ void ln_force_slice(const Params& p, int row_base, int part, uint32_t lane) {
+  const int row = row_base + static_cast<int>(lane);
+  bool mine = false;
+  if (row < p.M) {
+    const unsigned long long old = atomicOr(p.ln_state + row, 1ull << (32 + part));
+    mine = ln_published(old) == static_cast<unsigned>(p.ln_parts);
   }
+  const unsigned rows = __ballot_sync(0xffffffffu, mine);
+  if (rows == 0u) return;
+  __threadfence();  // the publishers' data after the complete count
+  ln_slice_rows(p, row_base, part, rows, mine, lane);
 }
 
 // wait sites (error word "where" low byte)
@@ -1030,6 +1157,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     uint8_t* stage = smem + C::EPI_OFFSET + (warp - 2) * C::EPI_BYTES_PER_WARP;
     uint32_t n_stores = 0;
     int it = 0;
+    // kBiasResidLnX: up to two slices whose normalisation is pending (first row, part; -1 = none)
+    int ln_row0 = -1, ln_part0 = 0, ln_row1 = -1, ln_part1 = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
@@ -1070,8 +1199,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
       // TMEM is released first: the next tile's main loop may proceed while
       // this warp publishes its statistics (and, when last, normalises rows).
-      if constexpr (EPI == kBiasResidLnX) ln_publish(p, ln_st, m0 + quad * 32, (n0 + half * HALF_N) / 128, lane);
+      if constexpr (EPI == kBiasResidLnX) {
+        const int part = (n0 + half * HALF_N) / 128;
+        ln_publish(p, ln_st, m0 + quad * 32, part, lane);
+        // pending slices, oldest first
+        for (int k = 0; k < 2 && ln_row0 >= 0 && ln_try_slice(p, ln_row0, ln_part0, lane); ++k) {
+          ln_row0 = ln_row1;
+          ln_part0 = ln_part1;
+          ln_row1 = -1;
+        }
+        if (ln_row1 >= 0) {  // both slots taken: the oldest cannot wait any longer
+          ln_force_slice(p, ln_row0, ln_part0, lane);
+          ln_row0 = ln_row1;
+          ln_part0 = ln_part1;
+          ln_row1 = -1;
+        }
+        if (ln_row0 < 0) {
+          ln_row0 = m0 + quad * 32;
+          ln_part0 = part;
+        } else {
+          ln_row1 = m0 + quad * 32;
+          ln_part1 = part;
+        }
+      }
       (void)ln_st;
+    }
+    if constexpr (EPI == kBiasResidLnX) {
+      if (!abort_flag) {
+        if (ln_row0 >= 0) ln_force_slice(p, ln_row0, ln_part0, lane);
+        if (ln_row1 >= 0) ln_force_slice(p, ln_row1, ln_part1, lane);
+      }
     }
     if (lane == 0) bulk_wait_all();  // stores complete before the CTA's shared memory goes away
   }

@@ -66,11 +66,15 @@ class OptimizerSettings:
     """Knobs of the B200 forward. None of them selects another backend."""
 
     # Fuse residual add + LayerNorm into the O-projection / FFN-out GEMM
-    # epilogue: in one tile when d_model is 64, 128 or 256, through per-row
-    # partial statistics across the CTA-pair tiles when d_model % 256 == 0
-    # (up to 4096); other widths use the GEMM residual epilogue followed by
-    # tk_layernorm.
+    # epilogue when d_model fits one tile row (64, 128 or 256).
     fused_ln_epilogue: bool = True
+    # Also fuse it for rows wider than a tile (d_model % 256 == 0, up to
+    # 4096: tk_gemm_resid_ln, per-row partial statistics across the CTA-pair
+    # tiles). Off by default: on one B200 at 65,536 x 1024 rows it measured
+    # 0.45 ms (O-projection, K 1024) and 0.62 ms (FFN-out, K 4096) against
+    # 0.24 ms and 0.54 ms for the in-place GEMM (TMA reduce-add) followed by
+    # tk_layernorm; the shape dispatch table can turn it on per shape.
+    fused_wide_ln: bool = False
     # Skip the one device->host sync that checks whether the mask is all-True.
     assume_dense_mask: bool = False
     # Synchronise after every forward and raise if a kernel's bounded
@@ -377,7 +381,8 @@ class OptimizedTransformer(nn.Module):
         T, d = res.shape
         ffn = u.shape[1]
         hd = self.head_dim
-        fused = self.settings.fused_ln_epilogue and tk_linear.fused_ln_supported(d)
+        fused = self.settings.fused_ln_epilogue and tk_linear.fused_ln_supported(d) and (
+            d in (64, 128, 256) or self.settings.fused_wide_ln)
         seq = S if lengths is not None else 0
         out = out_ws if out is None else out.view(T, d)
         run, lin = self._launch, tk_linear.linear
