@@ -117,6 +117,28 @@ TK_API int tk_gemm_resid_ln(const void* A, int64_t lda, const void* W, int64_t l
                             int64_t M, int64_t N, int64_t K,
                             void* workspace, int64_t workspace_bytes, void* stream);
 
+/* tk_gemm_resid_ln without the workspace argument. No counterpart in the
+ * reference: it is for callers that cannot allocate device memory -- a
+ * plugin whose host framework owns every device allocation, a serving loop
+ * that may not call the allocator once it runs, a caller with no memory
+ * budget left for a workspace -- and so cannot pass one. The scratch lives
+ * in an 8 MiB array inside the library (each GPU that loads the library
+ * holds it until the process exits); calls needing more than that
+ * (tk_gemm_resid_ln_workspace_bytes(M, N) > 8 MiB, e.g. M > 116,000 rows at
+ * N = 1024) return TK_ERR_UNSUPPORTED. Allocates nothing. The first call on
+ * a device looks the array's address up on that device (the caller's
+ * current one), so make it before any stream capture. Every call on a
+ * device shares the one array and clears its per-row counters before its
+ * kernel runs: calls that overlap on the GPU race with each other. Other
+ * arguments and results as tk_gemm_resid_ln; N in {64, 128, 256} needs no
+ * scratch and runs tk_gemm. */
+TK_API int tk_gemm_resid_ln_static(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                                   const float* resid, int64_t ld_resid, float* sum_out, int64_t ld_sum,
+                                   const float* gamma, const float* beta, float eps,
+                                   void* out, int out_dtype, int64_t ldo,
+                                   const int32_t* row_len, int64_t seq_len,
+                                   int64_t M, int64_t N, int64_t K, void* stream);
+
 /* Attention forward. Replaces F.scaled_dot_product_attention
  * (src/optimized.py:615-624) and flash_attention (src/kernels.py:250-294),
  * with the same contract as the latter: q, k, v are fp16, logically

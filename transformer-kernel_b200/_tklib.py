@@ -50,6 +50,8 @@ SIGNATURES = {
     "tk_gemm_resid_ln_supported": (_I, [_I64, _I64, _I64]),
     "tk_gemm_resid_ln": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _F, _P, _I, _I64, _P, _I64,
                               _I64, _I64, _I64, _P, _I64, _P]),
+    "tk_gemm_resid_ln_static": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _F, _P, _I, _I64, _P,
+                                     _I64, _I64, _I64, _I64, _P]),
     "tk_peer_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
     "tk_peer_import": (_I, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
     "tk_peer_release": (_I, [_P]),

@@ -509,6 +509,61 @@ int tk_gemm_resid_ln(const void* A, int64_t lda, const void* W, int64_t ldw, con
   return launch_gemm_pair<tk::gemm::kBiasResidLnX>(ma, mw, ma, p, info, static_cast<cudaStream_t>(stream));
 }
 
+// --- the same GEMM + residual + LayerNorm, with no workspace argument ---------
+// For callers that cannot allocate device memory (see include/tk_b200.h):
+// the scratch is a file-scope device array of fixed size, which every GPU
+// that loads this library holds until the process exits. Host code cannot
+// use the array's name as a device address, so the entry point looks the
+// address up once per device with cudaGetSymbolAddress.
+namespace {
+constexpr int64_t kStaticLnScratchBytes = int64_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_ln_static_scratch[kStaticLnScratchBytes];
+std::mutex g_static_mu;
+void* g_static_scratch_ptr[64] = {};
+}  // namespace
+
+int tk_gemm_resid_ln_static(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                            const float* resid, int64_t ld_resid, float* sum_out, int64_t ld_sum, const float* gamma,
+                            const float* beta, float eps, void* out, int out_dtype, int64_t ldo,
+                            const int32_t* row_len, int64_t seq_len, int64_t M, int64_t N, int64_t K, void* stream) {
+  g_last_error.clear();
+  if (N == 64 || N == 128 || N == 256)  // one tile holds the whole row: no scratch at all
+    return tk_gemm(A, lda, W, ldw, bias, TK_EPI_BIAS_RESID_LN, resid, ld_resid, sum_out, ld_sum, gamma, beta, eps,
+                   out, out_dtype, ldo, row_len, seq_len, M, N, K, stream);
+  if (!wide_ln_shape(N))
+    return fail(TK_ERR_UNSUPPORTED, "tk_gemm_resid_ln_static: needs N in {64,128,256} or N %% 256 == 0 with "
+                "512 <= N <= 4096 (N=%lld)", (long long)N);
+  if (M < 0) return fail(TK_ERR_INVALID, "tk_gemm_resid_ln_static: M=%lld", (long long)M);
+  const int64_t need = tk_gemm_resid_ln_workspace_bytes(M, N);
+  if (need > kStaticLnScratchBytes)
+    return fail(TK_ERR_UNSUPPORTED, "tk_gemm_resid_ln_static: M=%lld rows of N=%lld need %lld bytes of scratch; the "
+                "built-in scratch holds %lld bytes (at most %lld rows at this N); use tk_gemm_resid_ln with a "
+                "workspace", (long long)M, (long long)N, (long long)need, (long long)kStaticLnScratchBytes,
+                (long long)(kStaticLnScratchBytes / (8 + (N / 128) * 8) - 64));
+  int dev;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(TK_ERR_CUDA, "device ordinal %d out of range", dev);
+  void* scratch = nullptr;
+  {
+    // set-up, once per device, with that device current (the caller's)
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (g_static_scratch_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_ln_static_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(scratch)");
+      g_static_scratch_ptr[dev] = ptr;
+    }
+    scratch = g_static_scratch_ptr[dev];
+  }
+  // The array keeps the last call's contents, whatever its shape: zero the
+  // per-row state words this call counts in (front of the array) first.
+  e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(align256(M * 8)), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch)");
+  return tk_gemm_resid_ln(A, lda, W, ldw, bias, resid, ld_resid, sum_out, ld_sum, gamma, beta, eps, out, out_dtype,
+                          ldo, row_len, seq_len, M, N, K, scratch, kStaticLnScratchBytes, stream);
+}
+
 int tk_stack_small_supported(int64_t d, int64_t heads, int64_t ffn, int64_t seq_len) {
   return d == 128 && ffn == 128 && (heads == 2 || heads == 4) && seq_len >= 1 && seq_len <= 128 ? 1 : 0;
 }
