@@ -68,6 +68,27 @@ TK_API int tk_layernorm(const void* x, int x_dtype, int64_t ld_x,
                  const int32_t* row_len, int64_t seq_len,
                  int64_t rows, int64_t d, void* stream);
 
+/* GEMM tile configurations. By default tk_gemm picks the tile by fixed
+ * rules (the 256 x 256 CTA-pair tile once there is a wave of them, else the
+ * widest single-CTA tile that still gives every SM a tile). A table of
+ * measured choices overrides them: tk_gemm_tiles_set records the variant for
+ * a GEMM shape (M, N, K, epilogue); later tk_gemm calls with the same
+ * (N, K, epilogue) use the entry whose M is nearest on a log scale, when the
+ * shape can take that variant (TK_EPI_BIAS_RESID_LN always keeps its
+ * one-tile row). Replaces the reference's measured per-shape dispatch table
+ * (src/dispatch.py:95-215), which selects settings from sweep results.
+ * tk_gemm_tiles_chosen returns the variant tk_gemm would run. */
+typedef enum tk_tiles {
+  TK_TILES_AUTO = 0,   /* the built-in rules                     */
+  TK_TILES_PAIR = 1,   /* 256 x 256 over a CTA pair (N % 256 == 0) */
+  TK_TILES_256 = 2,    /* 128 x 256 on one SM (N % 256 == 0)      */
+  TK_TILES_128 = 3,    /* 128 x 128 on one SM (N % 128 == 0)      */
+  TK_TILES_64 = 4      /* 128 x 64 on one SM                      */
+} tk_tiles;
+TK_API int tk_gemm_tiles_set(int64_t M, int64_t N, int64_t K, int epilogue, int variant);
+TK_API int tk_gemm_tiles_clear(void);
+TK_API int tk_gemm_tiles_chosen(int64_t M, int64_t N, int64_t K, int epilogue);
+
 /* out = epilogue(A[M,K] . W[N,K]^T + bias), fp16 operands, fp32 accumulate
  * on the tcgen05 tensor cores. Replaces F.linear (src/optimized.py:572, :627,
  * :632-636) plus the elementwise ops fused into its epilogue (GELU

@@ -57,3 +57,72 @@ def test_generator_cli_writes_a_loadable_table(tmp_path):
     table = dispatch.load_table(out)
     assert dispatch.lookup(table, batch_size=64, seq_len=128, d_model=128, heads=4, layers=4, ffn_dim=128,
                            causal=True)["median_ms"] == 0.1
+
+
+# ---- the per-shape sweep runner and the GEMM tile table ---------------------
+
+import stat  # noqa: E402
+
+import pytest  # noqa: E402
+
+import sweep  # noqa: E402
+
+
+def _fake_python(tmp_path, body):
+    """A stand-in interpreter for the runner's child: ignores its arguments."""
+    p = tmp_path / "fake_python.sh"
+    p.write_text("#!/bin/sh\n" + body + "\n")
+    p.chmod(p.stat().st_mode | stat.S_IEXEC)
+    return str(p)
+
+
+@pytest.mark.parametrize("body,status", [
+    ("echo '{\"variant\": \"pair\", \"ms\": 1.5}'; exit 0", "ok"),
+    ("echo '{\"variant\": \"pair\", \"ms\": 1.5, \"status\": \"accuracy_failed\"}'; exit 2", "accuracy_failed"),
+    ("echo boom >&2; exit 1", "error"),
+    ("sleep 5", "timeout"),
+])
+def test_run_case_classifies_like_the_reference(tmp_path, body, status):
+    res = sweep.run_case("gemm", "C2", timeout=0.5 if status == "timeout" else 60,
+                         python=_fake_python(tmp_path, body))
+    assert res["status"] == status and res["case"] == "C2"
+    if status == "ok":
+        assert res["records"] == [{"variant": "pair", "ms": 1.5}]
+    if status == "error":
+        assert "boom" in res["stderr_tail"]
+
+
+def test_gemm_shapes_follow_the_forward():
+    got = {g["gemm"]: (g["M"], g["N"], g["K"], g["epilogue"]) for g in sweep.gemm_shapes("C3")}
+    assert got == {"qkv": (65536, 3072, 1024, "bias"), "ffn_in": (65536, 4096, 1024, "gelu"),
+                   "o": (65536, 1024, 1024, "resid"), "ffn_out": (65536, 1024, 4096, "resid")}
+    # d_model 128 fuses its LayerNorm in one tile: no tile choice for O / FFN-out
+    assert {g["gemm"] for g in sweep.gemm_shapes("13")} == {"qkv", "ffn_in"}
+    # the out-of-core-scale shape is measured at a bounded M
+    assert all(g["M"] == sweep.GEMM_MAX_M for g in sweep.gemm_shapes("C5"))
+
+
+def test_build_gemm_tiles_keeps_the_fastest_accepted_variant(tmp_path):
+    rec = lambda v, ms, st="ok": {"gemm": "qkv", "M": 4096, "N": 3072, "K": 1024, "epilogue": "bias",  # noqa: E731
+                                  "shape_name": "C3", "variant": v, "ms": ms, "status": st}
+    f = tmp_path / "g.jsonl"
+    f.write_text(json.dumps({"kind": "gemm", "case": "C3", "status": "accuracy_failed",
+                             "records": [rec("auto", 1.0), rec("pair", 0.8), rec("bn64", 0.5, "accuracy_failed")]})
+                 + "\n" + json.dumps({"kind": "gemm", "case": "X", "status": "timeout", "records": [rec("bn128", 0.1)]})
+                 + "\n")
+    tiles = dispatch.build_gemm_tiles([f])
+    assert len(tiles) == 1
+    assert tiles[0]["variant"] == "pair" and tiles[0]["alternatives"] == {"auto": 1.0, "pair": 0.8}
+
+
+def test_apply_gemm_tiles_fills_the_library_table():
+    import _tklib as tk
+
+    table = {"gemm_tiles": [{"M": 4096, "N": 3072, "K": 1024, "epilogue": "bias", "variant": "pair"},
+                            {"M": 512, "N": 512, "K": 512, "epilogue": "resid", "variant": "auto"}]}
+    try:
+        assert dispatch.apply_gemm_tiles(table) == 1
+        with pytest.raises(tk.TKError):
+            tk.call("tk_gemm_tiles_set", 0, 1, 1, 0, 1)  # a bad entry is refused on the host
+    finally:
+        tk.lib().tk_gemm_tiles_clear()

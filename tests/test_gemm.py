@@ -313,3 +313,39 @@ def test_gemm_resid_ln_rejects_bad_workspace(cuda_device):
     rc = tk.lib().tk_gemm_resid_ln(16, K, 16, K, 16, 16, N, 16, N, 16, 16, 1e-5, 16, 1, N, None, 0, M, N, K,
                                    None, 0, None)
     assert rc == -1 and b"workspace" in tk.lib().tk_last_error()
+
+
+# ---- tile variants chosen through the measured table (tk_gemm_tiles_set) ----
+
+@pytest.mark.parametrize("M,N,K,epi", [(16384, 3072, 1024, "bias"), (16384, 4096, 1024, "gelu"),
+                                       (16384, 1024, 4096, "resid"), (512, 2048, 512, "gelu"), (777, 1536, 512, "bias")])
+def test_every_tile_variant_matches_the_reference(cuda_device, M, N, K, epi):
+    import _tklib as tk
+
+    a, w, b = operands(M, N, K, seed=N + K)
+    r = seeded(M, N, seed=5) if epi == "resid" else None
+    want = ref_linear(a, w, b)
+    if epi == "gelu":
+        want = F.gelu(want, approximate="none")
+    if epi == "resid":
+        want = r + want
+    code = tk_linear.EPILOGUES[epi]
+    ran = set()
+    try:
+        for v in ("pair", "bn256", "bn128", "bn64"):
+            tk.lib().tk_gemm_tiles_clear()
+            tk.call("tk_gemm_tiles_set", M, N, K, code, tk.TILES[v])
+            chosen = tk.lib().tk_gemm_tiles_chosen(M, N, K, code)
+            if chosen != tk.TILES[v]:
+                continue
+            ran.add(v)
+            if epi == "resid":
+                out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), "resid", resid=r.cuda())
+                torch.testing.assert_close(out.cpu(), want, atol=1e-4, rtol=1e-4, msg=v)
+            else:
+                out = tk_linear.linear(a.cuda(), w.cuda(), b.cuda(), epi)
+                tol = dict(atol=2e-4, rtol=1e-3) if epi == "gelu" else dict(atol=2e-3, rtol=2e-2)
+                torch.testing.assert_close(out.float().cpu(), want, **tol, msg=v)
+    finally:
+        tk.lib().tk_gemm_tiles_clear()
+    assert "bn64" in ran and ("pair" in ran) == (N % 256 == 0)

@@ -20,6 +20,7 @@ LIB_PATH = HERE / "libtk_b200.so"
 TK_OK = 0
 TK_F32, TK_F16 = 0, 1
 EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESID, EPI_BIAS_RESID_LN = 0, 1, 2, 3
+TILES = {"auto": 0, "pair": 1, "bn256": 2, "bn128": 3, "bn64": 4}
 
 STATUS_NAMES = {
     -1: "TK_ERR_INVALID",
@@ -52,6 +53,9 @@ SIGNATURES = {
                               _I64, _I64, _I64, _P, _I64, _P]),
     "tk_gemm_resid_ln_static": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _F, _P, _I, _I64, _P,
                                      _I64, _I64, _I64, _I64, _P]),
+    "tk_gemm_tiles_set": (_I, [_I64, _I64, _I64, _I, _I]),
+    "tk_gemm_tiles_clear": (_I, []),
+    "tk_gemm_tiles_chosen": (_I, [_I64, _I64, _I64, _I]),
     "tk_peer_export": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
     "tk_peer_import": (_I, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
     "tk_peer_release": (_I, [_P]),

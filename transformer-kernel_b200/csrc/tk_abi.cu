@@ -7,10 +7,12 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "tk_attn.cuh"
 #include "tk_attn_wide.cuh"
@@ -240,11 +242,89 @@ int pick_bn(int epi, int64_t M, int64_t N, int sms) {
   return N % 32 == 0 ? 64 : 0;  // a 64-wide tile masks a trailing half tile
 }
 
+// Measured tile configurations (tk_gemm_tiles_set): for a GEMM's (N, K,
+// epilogue), the entry whose M is nearest on a log scale names the variant;
+// a variant the shape cannot take is ignored, as is an empty table.
+struct TileEntry {
+  int64_t M, N, K;
+  int epi, variant;
+};
+std::mutex g_tiles_mu;
+std::vector<TileEntry> g_tiles;
+
+int table_variant(int epi, int64_t M, int64_t N, int64_t K) {
+  std::lock_guard<std::mutex> lk(g_tiles_mu);
+  int best = TK_TILES_AUTO;
+  double best_d = 1e30;
+  for (const TileEntry& t : g_tiles) {
+    if (t.N != N || t.K != K || t.epi != epi) continue;
+    const double dd = std::fabs(std::log(static_cast<double>(t.M)) - std::log(static_cast<double>(M)));
+    if (dd < best_d) {
+      best_d = dd;
+      best = t.variant;
+    }
+  }
+  return best;
+}
+
+// (pair, tile width) for a GEMM: the table's variant when it applies, else
+// the built-in rules.
+void choose_tiles(int epi, int64_t M, int64_t N, int64_t K, int sms, bool* pair, int* bn) {
+  const int v = epi == TK_EPI_BIAS_RESID_LN ? TK_TILES_AUTO : table_variant(epi, M, N, K);
+  if (v == TK_TILES_PAIR && N % 256 == 0) {
+    *pair = true;
+    *bn = 128;
+    return;
+  }
+  if ((v == TK_TILES_256 && N % 256 == 0) || (v == TK_TILES_128 && N % 128 == 0) || v == TK_TILES_64) {
+    *pair = false;
+    *bn = v == TK_TILES_256 ? 256 : v == TK_TILES_128 ? 128 : 64;
+    return;
+  }
+  *pair = use_pair(epi, M, N, sms);
+  *bn = *pair ? 128 : pick_bn(epi, M, N, sms);  // pair: each CTA stages 128 rows of W
+}
+
 }  // namespace
 
 extern "C" {
 
 const char* tk_last_error(void) { return g_last_error.c_str(); }
+
+int tk_gemm_tiles_set(int64_t M, int64_t N, int64_t K, int epilogue, int variant) {
+  g_last_error.clear();
+  if (M <= 0 || N <= 0 || K <= 0 || epilogue < TK_EPI_BIAS || epilogue > TK_EPI_BIAS_RESID_LN ||
+      variant < TK_TILES_AUTO || variant > TK_TILES_64)
+    return fail(TK_ERR_INVALID, "tk_gemm_tiles_set: bad entry M=%lld N=%lld K=%lld epilogue=%d variant=%d",
+                (long long)M, (long long)N, (long long)K, epilogue, variant);
+  std::lock_guard<std::mutex> lk(g_tiles_mu);
+  for (TileEntry& t : g_tiles) {
+    if (t.M == M && t.N == N && t.K == K && t.epi == epilogue) {
+      t.variant = variant;
+      return TK_OK;
+    }
+  }
+  if (g_tiles.size() >= 4096) return fail(TK_ERR_UNSUPPORTED, "tk_gemm_tiles_set: table full (4096 entries)");
+  g_tiles.push_back(TileEntry{M, N, K, epilogue, variant});
+  return TK_OK;
+}
+
+int tk_gemm_tiles_clear(void) {
+  std::lock_guard<std::mutex> lk(g_tiles_mu);
+  g_tiles.clear();
+  return TK_OK;
+}
+
+int tk_gemm_tiles_chosen(int64_t M, int64_t N, int64_t K, int epilogue) {
+  g_last_error.clear();
+  int dev;
+  DeviceInfo* info;
+  if (int st = current_device(&dev, &info)) return st;
+  bool pair = false;
+  int bn = 0;
+  choose_tiles(epilogue, M, N, K, info->sms, &pair, &bn);
+  return pair ? TK_TILES_PAIR : bn == 256 ? TK_TILES_256 : bn == 128 ? TK_TILES_128 : bn == 64 ? TK_TILES_64 : 0;
+}
 
 const char* tk_version(void) { return "tk_b200 0.1 (sm_100a)"; }
 
@@ -368,8 +448,9 @@ int tk_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
   int dev;
   DeviceInfo* info;
   if (int st = current_device(&dev, &info)) return st;
-  const bool pair = use_pair(epilogue, M, N, info->sms);
-  const int bn = pair ? 128 : pick_bn(epilogue, M, N, info->sms);  // pair: each CTA stages 128 rows of W
+  bool pair = false;
+  int bn = 0;
+  choose_tiles(epilogue, M, N, K, info->sms, &pair, &bn);
   if (bn == 0) return fail(TK_ERR_UNSUPPORTED, "tk_gemm: N=%lld has no tile width", (long long)N);
 
   CUtensorMap ma, mw;

@@ -9,9 +9,15 @@ line per shape carrying the shape, the median forward time and the
 ``OptimizerSettings`` it ran with); the generator keeps the fastest record
 per shape and writes the table, and ``settings_for(config)`` applies it.
 
-    python bench.py --sweep all > a.jsonl
-    python bench.py --sweep all --set fused_small_stack=False > b.jsonl
-    python transformer-kernel_b200/dispatch.py a.jsonl b.jsonl --out dispatch.json
+    python transformer-kernel_b200/sweep.py model --out model.jsonl
+    python transformer-kernel_b200/sweep.py gemm --out gemm.jsonl
+    python transformer-kernel_b200/dispatch.py model.jsonl --gemm gemm.jsonl --out dispatch.json
+
+(``bench.py --sweep`` lines are accepted as model records too.) The table
+also carries ``gemm_tiles``: per measured GEMM shape (M, N, K, epilogue) the
+fastest tile variant whose output agreed with the built-in choice; the
+drop-in pushes them into ``libtk_b200`` (``tk_gemm_tiles_set``) once per
+process, where ``tk_gemm`` consults them before its built-in rules.
 
 Rules (as in the reference):
   * only ``OptimizerSettings`` fields are applied; other keys stay in the
@@ -22,8 +28,7 @@ Rules (as in the reference):
 Unlike the reference's settings, none of these select another backend or a
 lower precision: every combination runs the same B200 kernels with the same
 numerics (the test suite checks each path against the oracle), so the table
-only trades speed. The library's own tile choices (GEMM tile width, CTA-pair
-kernel, programmatic launch) are made per call inside ``libtk_b200``.
+only trades speed.
 """
 
 from __future__ import annotations
@@ -66,7 +71,8 @@ def load_table(path: Optional[pathlib.Path] = None) -> Optional[dict]:
 
 
 def lookup(table: dict, **shape) -> Optional[dict]:
-    """Table entry for a shape given as SHAPE_FIELDS keyword arguments."""
+    """The measured entry whose key is this shape's (fields as in
+    SHAPE_FIELDS), or None when the sweep never ran the shape."""
     return (table.get("entries") or {}).get(shape_key(**shape))
 
 
@@ -104,17 +110,35 @@ def settings_for(config, table: Optional[dict] = None, base=None, explicit: Iter
     return dataclasses.replace(base, **applicable_settings(entry.get("settings") or {}, explicit))
 
 
+def _records(path: pathlib.Path):
+    """Sweep records of a JSON-lines file: ``bench.py --sweep`` lines as they
+    are, ``sweep.py`` case lines unwrapped (only cases that ran to the end;
+    records that failed their accuracy check are dropped)."""
+    for line in path.read_text().splitlines():
+        line = line.strip()
+        if not line.startswith("{"):
+            continue
+        try:
+            item = json.loads(line)
+        except ValueError:
+            continue
+        if "records" in item:
+            if item.get("status") not in ("ok", "accuracy_failed"):
+                continue
+            for rec in item["records"]:
+                if rec.get("status", "ok") == "ok":
+                    yield rec
+        elif item.get("status", "ok") == "ok":
+            yield item
+
+
 def build_entries(paths: Iterable[pathlib.Path]) -> Dict[str, dict]:
     """Fastest sweep record per shape over JSON-line files written by
-    ``bench.py --sweep``."""
+    ``sweep.py model`` or ``bench.py --sweep``."""
     entries: Dict[str, dict] = {}
     for path in paths:
         path = pathlib.Path(path)
-        for line in path.read_text().splitlines():
-            line = line.strip()
-            if not line.startswith("{"):
-                continue
-            record = json.loads(line)
+        for record in _records(path):
             ms, settings, shape = record.get("ms"), record.get("settings"), record.get("shape")
             if ms is None or not settings or not shape:
                 continue
@@ -129,25 +153,76 @@ def build_entries(paths: Iterable[pathlib.Path]) -> Dict[str, dict]:
     return dict(sorted(entries.items()))
 
 
+def build_gemm_tiles(paths: Iterable[pathlib.Path]) -> list:
+    """Fastest accepted tile variant per GEMM shape (M, N, K, epilogue) over
+    ``sweep.py gemm`` files, with every variant's time for provenance."""
+    best: Dict[tuple, dict] = {}
+    for path in paths:
+        for rec in _records(pathlib.Path(path)):
+            if "variant" not in rec or rec.get("ms") is None:
+                continue
+            key = (rec["M"], rec["N"], rec["K"], rec["epilogue"])
+            entry = best.setdefault(key, {"M": rec["M"], "N": rec["N"], "K": rec["K"], "epilogue": rec["epilogue"],
+                                          "gemm": rec.get("gemm"), "shape_name": rec.get("shape_name"),
+                                          "variant": None, "ms": None, "alternatives": {}})
+            entry["alternatives"][rec["variant"]] = round(rec["ms"], 5)
+            if entry["ms"] is None or rec["ms"] < entry["ms"]:
+                entry["variant"], entry["ms"] = rec["variant"], rec["ms"]
+    return [best[k] for k in sorted(best)]
+
+
+_APPLIED = False
+
+
+def apply_gemm_tiles(table: Optional[dict]) -> int:
+    """Push the table's GEMM tile choices into the library (replacing any
+    there); returns the number of entries set."""
+    import _tklib as tk
+    import linear
+
+    tk.lib().tk_gemm_tiles_clear()
+    n = 0
+    for e in (table or {}).get("gemm_tiles") or []:
+        if e.get("variant") in (None, "auto"):
+            continue
+        tk.call("tk_gemm_tiles_set", e["M"], e["N"], e["K"], linear.EPILOGUES[e["epilogue"]], tk.TILES[e["variant"]])
+        n += 1
+    return n
+
+
+def ensure_applied() -> None:
+    """Once per process: the packaged table's GEMM tile choices go to the
+    library (called by the drop-in when it first builds its weights)."""
+    global _APPLIED
+    if not _APPLIED:
+        _APPLIED = True
+        apply_gemm_tiles(load_table())
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    parser.add_argument("results", nargs="+", help="JSON-line files written by bench.py --sweep")
+    parser.add_argument("results", nargs="*", help="model sweep records (sweep.py model, bench.py --sweep)")
+    parser.add_argument("--gemm", nargs="*", default=[], help="GEMM sweep records (sweep.py gemm)")
     parser.add_argument("--out", default=str(DEFAULT_TABLE_PATH))
     args = parser.parse_args()
     paths = [pathlib.Path(p) for p in args.results]
+    gpaths = [pathlib.Path(p) for p in args.gemm]
     entries = build_entries(paths)
-    if not entries:
+    tiles = build_gemm_tiles(gpaths)
+    if not entries and not tiles:
         print("no sweep records found in the given files")
         return 1
-    payload = {"schema": 1, "generated_at": time.strftime("%Y-%m-%dT%H:%M:%S%z"),
-               "sources": [p.name for p in paths], "entries": entries}
+    payload = {"schema": 2, "generated_at": time.strftime("%Y-%m-%dT%H:%M:%S%z"),
+               "sources": [p.name for p in paths + gpaths], "entries": entries, "gemm_tiles": tiles}
     out = pathlib.Path(args.out)
     out.parent.mkdir(parents=True, exist_ok=True)
     out.write_text(json.dumps(payload, indent=2) + "\n")
-    width = max(len(k) for k in entries)
+    width = max([len(k) for k in entries] or [1])
     for key, entry in entries.items():
         print(f"{key:<{width}}  {entry['median_ms']:>9.4f} ms  {entry['settings']}  <- {entry['source']}")
-    print(f"\nwrote {out} ({len(entries)} shapes from {len(paths)} files)")
+    for t in tiles:
+        print(f"gemm {t['M']}x{t['N']}x{t['K']} {t['epilogue']}: {t['variant']} {t['ms']:.4f} ms  {t['alternatives']}")
+    print(f"\nwrote {out} ({len(entries)} shapes, {len(tiles)} GEMM shapes)")
     return 0
 
 

@@ -197,6 +197,9 @@ class OptimizedTransformer(nn.Module):
         key = (ref.device, ref.dtype, ref.data_ptr())
         if self._weight_cache is not None and self._weight_cache_key == key:
             return self._weight_cache
+        import dispatch
+
+        dispatch.ensure_applied()  # the measured GEMM tile table, once per process
         built = []
         with torch.no_grad():
             f16 = lambda t: t.detach().to(torch.float16).contiguous()  # noqa: E731
