@@ -108,11 +108,14 @@ def test_build_gemm_tiles_keeps_the_fastest_accepted_variant(tmp_path):
     f = tmp_path / "g.jsonl"
     f.write_text(json.dumps({"kind": "gemm", "case": "C3", "status": "accuracy_failed",
                              "records": [rec("auto", 1.0), rec("pair", 0.8), rec("bn64", 0.5, "accuracy_failed")]})
+                 + "\n" + json.dumps({"kind": "gemm", "case": "C3b", "status": "ok",
+                                       "records": [dict(rec("auto", 2.0), M=8192), dict(rec("bn128", 1.98), M=8192)]})
                  + "\n" + json.dumps({"kind": "gemm", "case": "X", "status": "timeout", "records": [rec("bn128", 0.1)]})
                  + "\n")
-    tiles = dispatch.build_gemm_tiles([f])
-    assert len(tiles) == 1
-    assert tiles[0]["variant"] == "pair" and tiles[0]["alternatives"] == {"auto": 1.0, "pair": 0.8}
+    tiles = {t["M"]: t for t in dispatch.build_gemm_tiles([f])}
+    assert len(tiles) == 2
+    assert tiles[4096]["variant"] == "pair" and tiles[4096]["alternatives"] == {"auto": 1.0, "pair": 0.8}
+    assert tiles[8192]["variant"] == "auto"  # 1% faster is a tie: the built-in choice stays
 
 
 def test_apply_gemm_tiles_fills_the_library_table():

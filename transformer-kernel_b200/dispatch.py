@@ -153,9 +153,14 @@ def build_entries(paths: Iterable[pathlib.Path]) -> Dict[str, dict]:
     return dict(sorted(entries.items()))
 
 
+TILE_TIE = 0.03  # a variant must beat the built-in choice by more than this fraction
+
+
 def build_gemm_tiles(paths: Iterable[pathlib.Path]) -> list:
     """Fastest accepted tile variant per GEMM shape (M, N, K, epilogue) over
-    ``sweep.py gemm`` files, with every variant's time for provenance."""
+    ``sweep.py gemm`` files, with every variant's time for provenance. A
+    variant within TILE_TIE of the built-in choice ("auto") is a tie and
+    leaves the built-in choice in place (launch-time noise is a few percent)."""
     best: Dict[tuple, dict] = {}
     for path in paths:
         for rec in _records(pathlib.Path(path)):
@@ -168,6 +173,10 @@ def build_gemm_tiles(paths: Iterable[pathlib.Path]) -> list:
             entry["alternatives"][rec["variant"]] = round(rec["ms"], 5)
             if entry["ms"] is None or rec["ms"] < entry["ms"]:
                 entry["variant"], entry["ms"] = rec["variant"], rec["ms"]
+    for entry in best.values():
+        auto = entry["alternatives"].get("auto")
+        if auto is not None and entry["ms"] > (1.0 - TILE_TIE) * auto:
+            entry["variant"], entry["ms"] = "auto", auto
     return [best[k] for k in sorted(best)]
 
 
