@@ -116,6 +116,11 @@ def test_build_gemm_tiles_keeps_the_fastest_accepted_variant(tmp_path):
     assert len(tiles) == 2
     assert tiles[4096]["variant"] == "pair" and tiles[4096]["alternatives"] == {"auto": 1.0, "pair": 0.8}
     assert tiles[8192]["variant"] == "auto"  # 1% faster is a tie: the built-in choice stays
+    small = tmp_path / "small.jsonl"
+    small.write_text(json.dumps({"kind": "gemm", "case": "C2", "status": "ok",
+                                 "records": [dict(rec("auto", 1.0), M=512), dict(rec("bn64", 0.5), M=512)]}) + "\n")
+    # 512 x 3072 x 1024 is launch-bound: the isolated winner does not replace the built-in choice
+    assert dispatch.build_gemm_tiles([small])[0]["variant"] == "auto"
 
 
 def test_apply_gemm_tiles_fills_the_library_table():
@@ -124,7 +129,7 @@ def test_apply_gemm_tiles_fills_the_library_table():
     table = {"gemm_tiles": [{"M": 4096, "N": 3072, "K": 1024, "epilogue": "bias", "variant": "pair"},
                             {"M": 512, "N": 512, "K": 512, "epilogue": "resid", "variant": "auto"}]}
     try:
-        assert dispatch.apply_gemm_tiles(table) == 1
+        assert dispatch.apply_gemm_tiles(table) == 2  # the built-in choice is an entry too
         with pytest.raises(tk.TKError):
             tk.call("tk_gemm_tiles_set", 0, 1, 1, 0, 1)  # a bad entry is refused on the host
     finally:

@@ -154,6 +154,12 @@ def build_entries(paths: Iterable[pathlib.Path]) -> Dict[str, dict]:
 
 
 TILE_TIE = 0.03  # a variant must beat the built-in choice by more than this fraction
+# GEMMs at or below this M*N*K are launch-bound: the library launches them
+# with programmatic dependent launch, overlapped with their neighbours, so
+# their isolated back-to-back timing does not predict their time inside a
+# forward (measured: C2 forward 0.213 -> 0.244 ms with isolated-sweep picks).
+# They keep the built-in choice.
+SMALL_GEMM_MNK = 8.6e9
 
 
 def build_gemm_tiles(paths: Iterable[pathlib.Path]) -> list:
@@ -175,8 +181,11 @@ def build_gemm_tiles(paths: Iterable[pathlib.Path]) -> list:
                 entry["variant"], entry["ms"] = rec["variant"], rec["ms"]
     for entry in best.values():
         auto = entry["alternatives"].get("auto")
-        if auto is not None and entry["ms"] > (1.0 - TILE_TIE) * auto:
+        small = float(entry["M"]) * entry["N"] * entry["K"] <= SMALL_GEMM_MNK
+        if auto is not None and (small or entry["ms"] > (1.0 - TILE_TIE) * auto):
             entry["variant"], entry["ms"] = "auto", auto
+            if small:
+                entry["note"] = "launch-bound: built-in choice kept"
     return [best[k] for k in sorted(best)]
 
 
@@ -192,8 +201,10 @@ def apply_gemm_tiles(table: Optional[dict]) -> int:
     tk.lib().tk_gemm_tiles_clear()
     n = 0
     for e in (table or {}).get("gemm_tiles") or []:
-        if e.get("variant") in (None, "auto"):
+        if e.get("variant") is None:
             continue
+        # built-in ("auto") choices are entries too: a measured M that kept the
+        # built-in choice must be the nearest match for the Ms around it
         tk.call("tk_gemm_tiles_set", e["M"], e["N"], e["K"], linear.EPILOGUES[e["epilogue"]], tk.TILES[e["variant"]])
         n += 1
     return n
