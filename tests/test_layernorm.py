@@ -103,3 +103,31 @@ def test_layernorm_large_rows(cuda_device, d, x_dtype, out_dtype, pad_cols):
         torch.testing.assert_close(y.cpu(), ref, atol=1e-5, rtol=1e-5)
     else:
         torch.testing.assert_close(y.float().cpu(), ref, atol=2e-3, rtol=2e-2)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.float32])
+def test_layernorm_large_rows_copy_and_padding(cuda_device, out_dtype):
+    """The forward's LayerNorm at large row counts (the persistent prefetching
+    kernel): the copy of the input rows into the residual buffer is exact,
+    and rows past their sequence's prefix length come out as zeros."""
+    import _tklib as tk
+
+    S, B, d = 128, 40, 1024
+    rows = S * B
+    x = seeded(rows, d, seed=41, scale=3.0)
+    w = seeded(d, seed=42, scale=0.5) + 1.0
+    b = seeded(d, seed=43, scale=0.5)
+    lengths = ((torch.arange(B, dtype=torch.int32) * 37) % (S + 1)).cuda()
+    copy = torch.full((rows, d), 5.0, device="cuda")
+    out = torch.empty(rows, d, dtype=out_dtype, device="cuda")
+    tk.call("tk_layernorm", x.data_ptr(), tk.TK_F32, d, None, 0, 0, copy.data_ptr(), d, w.data_ptr(), b.data_ptr(),
+            1e-5, out.data_ptr(), tk.dtype_code(out_dtype), d, lengths.data_ptr(), S, rows, d,
+            tk.stream_handle(cuda_device))
+    torch.cuda.synchronize()
+    torch.testing.assert_close(copy, x, atol=0, rtol=0)
+    pad = ((torch.arange(rows) % S) >= lengths.cpu().repeat_interleave(S))
+    got = out.float().cpu()
+    assert torch.all(got[pad] == 0)
+    ref = layer_norm_reference(x.cpu(), w.cpu(), b.cpu(), 1e-5, torch.float32)
+    tol = dict(atol=2e-3, rtol=2e-2) if out_dtype == torch.float16 else dict(atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(got[~pad], ref[~pad], **tol)

@@ -389,7 +389,25 @@ int tk_layernorm(const void* x, int x_dtype, int64_t ld_x, const void* y, int y_
 
   cudaError_t e = cudaSuccess;
   const bool small = static_cast<double>(rows) * d <= kSmallLnElements;
-  if (d <= 1024) {
+  if (d <= 1024 && y == nullptr && a.vec && x_dtype == TK_F32 && rows >= 8 * info->sms) {
+    // the forward's LayerNorm (fp32 rows in, no residual branch): persistent
+    // grid, each warp prefetching its next row (two 256-thread CTAs per SM)
+    const int64_t cap = static_cast<int64_t>(info->sms) * 2;
+    const int64_t blocks = (rows + 7) / 8;
+    const int grid = static_cast<int>(blocks < cap ? blocks : cap);
+    auto go = [&](auto kern) { return launch(kern, dim3(grid), dim3(256), 0, s, small, a); };
+    if (of) {
+      if (d <= 128) e = go(tk::ln::ln_warp_rows_prefetch<1, float, float, float>);
+      else if (d <= 256) e = go(tk::ln::ln_warp_rows_prefetch<2, float, float, float>);
+      else if (d <= 512) e = go(tk::ln::ln_warp_rows_prefetch<4, float, float, float>);
+      else e = go(tk::ln::ln_warp_rows_prefetch<8, float, float, float>);
+    } else {
+      if (d <= 128) e = go(tk::ln::ln_warp_rows_prefetch<1, float, float, __half>);
+      else if (d <= 256) e = go(tk::ln::ln_warp_rows_prefetch<2, float, float, __half>);
+      else if (d <= 512) e = go(tk::ln::ln_warp_rows_prefetch<4, float, float, __half>);
+      else e = go(tk::ln::ln_warp_rows_prefetch<8, float, float, __half>);
+    }
+  } else if (d <= 1024) {
     const int64_t warps_needed = rows;
     int64_t blocks = (warps_needed + 7) / 8;
     const int64_t cap = static_cast<int64_t>(info->sms) * 16;

@@ -158,6 +158,79 @@ __global__ void __launch_bounds__(256, 3) ln_warp_rows(Args a) {
   }
 }
 
+// The forward's LayerNorm (no residual branch, vector-aligned rows, d <= NV *
+// 128): the same row math as ln_warp_rows, on a persistent grid where each
+// warp loads its next row while it reduces, normalises and stores the
+// current one, so a row's loads are always in flight behind the previous
+// row's arithmetic and stores (one row at a time leaves the loads idle for
+// the whole reduction).
+template <int NV, typename TX, typename TS, typename TH>
+__global__ void __launch_bounds__(256, 2) ln_warp_rows_prefetch(Args a) {
+  grid_dep_wait();  // the previous kernel's outputs are complete and visible
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int d = static_cast<int>(a.d);
+  const float inv_d = 1.f / static_cast<float>(d);
+  int64_t row = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  float cur[NV][4], nxt[NV][4];
+  auto load_row = [&](int64_t r, float (&v)[NV][4]) {
+    const TX* xr = static_cast<const TX*>(a.x) + r * a.ld_x;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      Vec4<TX>::load(xr + c, true, max(0, min(4, d - c)), v[i]);
+    }
+  };
+  if (row < a.rows) load_row(row, cur);
+  for (; row < a.rows; row += nwarps) {
+    const int64_t next = row + nwarps;
+    if (next < a.rows) load_row(next, nxt);  // in flight during this row's work
+    const bool pad = row_is_padding(a, row);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      const int n = max(0, min(4, d - c));
+      if (a.s != nullptr && n > 0) Vec4<TS>::store(static_cast<TS*>(a.s) + row * a.ld_s + c, true, n, cur[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) sum += cur[i][k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const float mean = sum * inv_d;
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 4;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float t = (c + k < d) ? cur[i][k] - mean : 0.f;
+        sq += t * t;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float rstd = rsqrtf(sq * inv_d + a.eps);
+    TH* hr = static_cast<TH*>(a.h) + row * a.ld_h;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 4;
+      const int n = max(0, min(4, d - c));
+      if (n <= 0) continue;
+      float g[4], b[4], o[4];
+      Vec4<float>::load(a.gamma + c, true, n, g);
+      Vec4<float>::load(a.beta + c, true, n, b);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o[k] = pad ? 0.f : (cur[i][k] - mean) * rstd * g[k] + b[k];
+      Vec4<TH>::store(hr + c, true, n, o);
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) cur[i][k] = nxt[i][k];
+  }
+}
+
 // One 256-thread CTA per row, d <= 8192 (8 groups of 4 per thread).
 template <typename TX, typename TY, typename TS, typename TH>
 __global__ void __launch_bounds__(256) ln_cta_rows(Args a) {
