@@ -265,3 +265,19 @@ def test_small_stack_kernel(cuda_device, cfg, padding):
     with torch.inference_mode():
         out2 = per_layer(x.cuda(), mask.cuda()).cpu()
     torch.testing.assert_close(out, out2, atol=2e-3, rtol=2e-2)
+
+
+def test_forward_from_host_changing_slice_shapes(cuda_device):
+    """One model, consecutive streamed calls whose slices change shape (the
+    slots are rebuilt while the previous call's copies may be in flight)."""
+    cfg = StackConfig(6, 128, 256, 4, 512, 2, False)
+    _, model = build(cfg)
+    x, mask = generate_random_case(cfg, 13)
+    with torch.inference_mode():
+        want = model(x.cuda(), mask.cuda()).cpu()
+        outs = [model.forward_from_host(x.pin_memory(), mask, chunks=c).clone() for c in (3, 2, 6, 3)]
+        part = model.forward_from_host(x[1:4].pin_memory(), mask[1:4], chunks=2)
+        torch.cuda.synchronize()
+    for o in outs:
+        torch.testing.assert_close(o, want, atol=0, rtol=0)
+    torch.testing.assert_close(part, want[1:4], atol=0, rtol=0)

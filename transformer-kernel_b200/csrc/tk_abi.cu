@@ -160,6 +160,7 @@ int allocation_range(const void* ptr, CUdeviceptr* base, size_t* size) {
 // Imported peer allocations: one mapping per exported allocation, counted.
 struct PeerMap {
   void* base;
+  size_t size;
   int refs;
 };
 std::mutex g_peer_mu;
@@ -866,8 +867,17 @@ int tk_peer_import(const void* handle, int64_t offset, void** ptr) {
     void* base = nullptr;
     cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
     if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
-    it = g_peer_maps.emplace(key, PeerMap{base, 0}).first;
+    CUdeviceptr b = 0;
+    size_t size = 0;
+    if (int st = allocation_range(base, &b, &size)) {
+      cudaIpcCloseMemHandle(base);
+      return st;
+    }
+    it = g_peer_maps.emplace(key, PeerMap{base, size, 0}).first;
   }
+  if (static_cast<size_t>(offset) >= it->second.size)
+    return fail(TK_ERR_INVALID, "tk_peer_import: offset %lld beyond the %zu-byte allocation", (long long)offset,
+                it->second.size);
   ++it->second.refs;
   *ptr = static_cast<char*>(it->second.base) + offset;
   return TK_OK;
@@ -876,10 +886,12 @@ int tk_peer_import(const void* handle, int64_t offset, void** ptr) {
 int tk_peer_release(void* ptr) {
   g_last_error.clear();
   std::lock_guard<std::mutex> lk(g_peer_mu);
-  // the mapping whose range holds ptr: the largest base not above it
+  // the mapping whose range holds ptr
   auto best = g_peer_maps.end();
+  const uintptr_t q = reinterpret_cast<uintptr_t>(ptr);
   for (auto it = g_peer_maps.begin(); it != g_peer_maps.end(); ++it) {
-    if (it->second.base <= ptr && (best == g_peer_maps.end() || it->second.base > best->second.base)) best = it;
+    const uintptr_t b = reinterpret_cast<uintptr_t>(it->second.base);
+    if (q >= b && q < b + it->second.size) best = it;
   }
   if (best == g_peer_maps.end()) return fail(TK_ERR_INVALID, "tk_peer_release: %p is not in an imported mapping", ptr);
   if (--best->second.refs == 0) {

@@ -127,6 +127,7 @@ class BatchSplitForward:
         self.comp = torch.cuda.Stream(dev)
         self.cout = torch.cuda.Stream(dev)
         self._token = torch.zeros(1, dtype=torch.float32, device=dev)
+        self._closed = False
 
     def _fence(self) -> None:
         """Stream-ordered rendezvous of all ranks (tiny NCCL all-reduce on the
@@ -138,6 +139,8 @@ class BatchSplitForward:
     def step(self) -> Optional[torch.Tensor]:
         """This rank's share of one forward. Returns ``output`` on the home
         rank (complete once the current stream passes this point), else None."""
+        if self._closed:
+            raise tk.TKError("BatchSplitForward.step", -1, "called after close(): the peer buffers are unmapped")
         dev = self.device
         cur = torch.cuda.current_stream(dev)
         weights = self.model._weights()
@@ -181,4 +184,5 @@ class BatchSplitForward:
         for ptr in self._imported:
             tk.peer_release(ptr)
         self._imported = []
+        self._closed = True
         dist.barrier(group=self.group, device_ids=[self.device.index])

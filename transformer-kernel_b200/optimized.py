@@ -526,6 +526,13 @@ class OptimizedTransformer(nn.Module):
         ctx = getattr(self, "_stream_ctx", None)
         if ctx is not None and ctx["key"] == key:
             return ctx
+        if ctx is not None:
+            # the old slots may still be read and written by work queued on the
+            # old streams, which the caching allocator does not know about: let
+            # it finish before the buffers go back to the allocator
+            for name in ("h2d", "compute", "d2h"):
+                ctx[name].synchronize()
+            self._stream_ctx = None
         ffn = weights[0].ffn_in_w.shape[0]
         with torch.cuda.device(dev):
             slots = [{"x": torch.empty((cb, S, d), dtype=torch.float32, device=dev),
