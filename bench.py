@@ -605,6 +605,8 @@ def main() -> int:
                     help="torchrun split: micro-batches per rank (copy-in / forward / copy-out overlap)")
     ap.add_argument("--replicas", action="store_true",
                     help="torchrun: every rank runs the whole batch (weak scaling, no exchange)")
+    ap.add_argument("--split", action="store_true",
+                    help="run the batch-split path (the torchrun default) even on one GPU")
     ap.add_argument("--sweep", default="", help="comma-separated appendix cases (or 'all'): one JSON line each, "
                                                 "timed like the harness (median of CUDA-event samples)")
     ap.add_argument("--set", action="append", default=[], metavar="FIELD=VALUE",
@@ -636,7 +638,12 @@ def main() -> int:
         if world > 1:
             ap.error("--strong runs in one process; do not launch it under torchrun")
         return run_strong(args, cfg_tuple)
-    if world > 1 and not args.replicas:
+    if (world > 1 and not args.replicas) or args.split:
+        if world == 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29561")
+            os.environ.setdefault("RANK", "0")
+            os.environ.setdefault("WORLD_SIZE", "1")
         return run_split(args, cfg_tuple, world, rank, local)
     return run_single(args, cfg_tuple, world, rank, local)
 

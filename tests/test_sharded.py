@@ -202,3 +202,54 @@ def test_peer_export_import_copy_rows_between_processes(cuda_device):
         p.join(timeout=240)
         assert p.exitcode == 0
     assert [result.get(timeout=10), result.get(timeout=10)] == [True, True]
+
+
+def _free_port():
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("micro", [1, 3])
+def test_batch_split_one_rank_matches_single_gpu(cuda_device, micro):
+    """BatchSplitForward with a one-rank process group: the home buffers,
+    the micro-batched copy-in / forward / copy-out pipeline (graph replays
+    from the second step on) and the fences, against the one-GPU forward bit
+    for bit. (Several ranks need one GPU each; their peer mappings are
+    covered by the two-process IPC test.)"""
+    import torch.distributed as dist
+
+    import distributed
+    import optimized
+    from oracle import StackConfig, generate_random_case, init_params
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=cuda_device)
+    try:
+        cfg = StackConfig(7, 128, 256, 4, 512, 2, True)
+        model = optimized.OptimizedTransformer(cfg)
+        model.load_state_dict(init_params(cfg, seed=0), strict=True)
+        model = model.cuda().eval()
+        split = distributed.BatchSplitForward(model, (7, 128, 256), micro_batches=micro)
+        x, _ = generate_random_case(cfg, 31)
+        with torch.inference_mode():
+            want = model(x.cuda()).clone()
+            split.input.copy_(x)
+            for _ in range(4):
+                got = split.step()
+            torch.cuda.synchronize()
+            torch.testing.assert_close(got, want, atol=0, rtol=0)
+            x2, _ = generate_random_case(cfg, 32)
+            split.input.copy_(x2)
+            got2 = split.step().clone()
+            want2 = model(x2.cuda())
+            torch.cuda.synchronize()
+            torch.testing.assert_close(got2, want2, atol=0, rtol=0)
+        split.close()
+        with pytest.raises(Exception):
+            split.step()
+    finally:
+        dist.destroy_process_group()
