@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m = -INFINITY;  // running max, raw score units
       float l = 0.f;
       for (int j = 0; j < n_g; ++j, ++tiles) {
-        if (!mbar_wait(&s_full[g], tiles & 1, &abort_flag, p.wait_limit_ns)) {
+        if (!mbar_wait_warp(&s_full[g], tiles & 1, &abort_flag, p.wait_limit_ns)) {
           report_error(kDevWaitTimeout, kid * 256 + kSiteS);
           abort_flag = 1;
           ok = false;
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // PV_g of the previous tile reads P_g and writes O_g: it must be
         // complete before P_g is overwritten or O_g rescaled.
         if (tiles > 0) {
-          if (!mbar_wait(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+          if (!mbar_wait_warp(&pv_done[g], (tiles - 1) & 1, &abort_flag, p.wait_limit_ns)) {
             report_error(kDevWaitTimeout, kid * 256 + kSitePv);
             abort_flag = 1;
             ok = false;
@@ -548,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       // epilogue: O / l -> fp16 [b, q, h*HD + c]
       if (n_g > 0) {
-        if (!mbar_wait(&o_full[g], o_uses & 1, &abort_flag, p.wait_limit_ns)) {
+        if (!mbar_wait_warp(&o_full[g], o_uses & 1, &abort_flag, p.wait_limit_ns)) {
           report_error(kDevWaitTimeout, kid * 256 + kSiteO);
           abort_flag = 1;
           ok = false;

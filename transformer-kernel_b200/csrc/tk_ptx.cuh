@@ -120,6 +120,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// mbar_wait by all 32 lanes of a warp with one warp-uniform answer: the warp
+// goes on only if every lane saw the phase complete, so a lane that gave up
+// (time limit or abort) cannot leave the others alone at a warp-collective
+// instruction (tcgen05.ld / st, __syncwarp, vote).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, const volatile int* abort,
+                                               uint64_t limit_ns) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, limit_ns));
+}
+
 // ----------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), CTA-local destination, no multicast.
 // ----------------------------------------------------------------------------
