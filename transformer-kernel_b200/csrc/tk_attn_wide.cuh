@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < it.n; ++j) {
-      if (!mbar_wait(&s_full, j & 1, &abort_flag, p.wait_limit_ns)) {
+      if (!mbar_wait_warp(&s_full, j & 1, &abort_flag, p.wait_limit_ns)) {
         report_error(kDevWaitTimeout, kid * 256 + kSiteS);
         abort_flag = 1;
         ok = false;
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       // PV(j-1) reads P and writes O: complete before P is overwritten or O rescaled.
       if (j > 0) {
-        if (!mbar_wait(&pv_done, (j - 1) & 1, &abort_flag, p.wait_limit_ns)) {
+        if (!mbar_wait_warp(&pv_done, (j - 1) & 1, &abort_flag, p.wait_limit_ns)) {
           report_error(kDevWaitTimeout, kid * 256 + kSitePv);
           abort_flag = 1;
           ok = false;
@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // epilogue: O / l -> fp16 [b, q, h*HD + c]
     if (ok && it.n > 0) {
-      if (!mbar_wait(&o_full, 0, &abort_flag, p.wait_limit_ns)) {
+      if (!mbar_wait_warp(&o_full, 0, &abort_flag, p.wait_limit_ns)) {
         report_error(kDevWaitTimeout, kid * 256 + kSiteO);
         abort_flag = 1;
         ok = false;

@@ -826,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&acc_full[acc], acc_phase, &abort_flag, p.wait_limit_ns)) {
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, &abort_flag, p.wait_limit_ns)) {
         report_error(kDevWaitTimeout, kid * 256 + kSiteAccFull);
         abort_flag = 1;
         break;
@@ -894,7 +894,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float inv_n = 1.f / static_cast<float>(p.N);
           ln_part[(half * 2 + 0) * kBM + row_in_tile] = part_sum;
           mbar_arrive(&ln_bar[0]);
-          if (!mbar_wait(&ln_bar[0], ln_phase, &abort_flag, p.wait_limit_ns)) {
+          if (!mbar_wait_warp(&ln_bar[0], ln_phase, &abort_flag, p.wait_limit_ns)) {
             report_error(kDevWaitTimeout, kid * 256 + kSiteLn);
             abort_flag = 1;
             break;
@@ -914,7 +914,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ln_part[(half * 2 + 1) * kBM + row_in_tile] = part_sq;
           mbar_arrive(&ln_bar[1]);
-          if (!mbar_wait(&ln_bar[1], ln_phase, &abort_flag, p.wait_limit_ns)) {
+          if (!mbar_wait_warp(&ln_bar[1], ln_phase, &abort_flag, p.wait_limit_ns)) {
             report_error(kDevWaitTimeout, kid * 256 + kSiteLn);
             abort_flag = 1;
             break;
@@ -1172,7 +1172,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (nrow < p.M) prefetch_l2_bulk(p.resid + static_cast<int64_t>(nrow) * p.ld_resid + ncol, HALF_N * 4);
         }
       }
-      if (!mbar_wait_cluster(&acc_full[acc], acc_phase, &abort_flag, p.wait_limit_ns)) {
+      // warp-uniform: every lane must agree before the warp-collective TMEM loads
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[acc], acc_phase, &abort_flag, p.wait_limit_ns))) {
         report_error(kDevWaitTimeout, kid * 256 + kSiteAccFull);
         abort_flag = 1;
         break;

@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(bar);
     };
     auto wait_acc = [&]() -> bool {
-      if (!mbar_wait(&acc_full, nacc & 1, &abort_flag, p.wait_limit_ns)) {
+      if (!mbar_wait_warp(&acc_full, nacc & 1, &abort_flag, p.wait_limit_ns)) {
         fail(kSiteAcc);
         return false;
       }
@@ -486,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < H && ok; ++h) {
         const int b = h & 1;
         const uint32_t phase = b == 0 ? (nsf0++ & 1) : (nsf1++ & 1);
-        if (!mbar_wait(&s_full[b], phase, &abort_flag, p.wait_limit_ns)) {
+        if (!mbar_wait_warp(&s_full[b], phase, &abort_flag, p.wait_limit_ns)) {
           fail(kSiteS);
           break;
         }
@@ -529,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         signal(&p_full[b]);
       }
       if (!ok) break;
-      if (!mbar_wait(&attn_done, l & 1, &abort_flag, p.wait_limit_ns)) {
+      if (!mbar_wait_warp(&attn_done, l & 1, &abort_flag, p.wait_limit_ns)) {
         fail(kSiteAttn);
         break;
       }
