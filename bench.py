@@ -597,7 +597,7 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="bounded CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-chunks", type=int, default=0,
-                    help="batch slices of the streamed end-to-end forward (default: ~16+ sequences a slice, <= 4)")
+                    help="batch slices of the streamed end-to-end forward (default: ~16+ sequences a slice, <= 2)")
     ap.add_argument("--extras", default="auto",
                     help="comma-separated extra configurations measured after the main one (default: C1,C2,C4,C5 "
                          "on one GPU, C4,C5 split under torchrun); 'none' to skip")
@@ -663,7 +663,7 @@ def cpu_baseline(args, cfg_tuple):
 def e2e_chunks(args, batch):
     if args.e2e_chunks > 0:
         return args.e2e_chunks
-    return max(1, min(4, batch // 16))
+    return max(1, min(2, batch // 16))
 
 
 def extras_list(args, world):

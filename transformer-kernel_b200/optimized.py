@@ -438,7 +438,7 @@ class OptimizedTransformer(nn.Module):
         x_host: torch.Tensor,
         valid_token_mask: Optional[torch.Tensor] = None,
         out_host: Optional[torch.Tensor] = None,
-        chunks: int = 4,
+        chunks: int = 2,
         device: Optional[torch.device] = None,
     ) -> torch.Tensor:
         """Forward over a batch that lives in (pinned) host memory.
