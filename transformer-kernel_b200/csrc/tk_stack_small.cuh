@@ -45,6 +45,12 @@ constexpr int kAtomBytes = kRows * 64 * 2;       // 16 KB: 128 rows x one 64-col
 constexpr int kWRowsPerLayer = 768;              // packed weight rows: Wqkv 384, Wo 128, W1 128, W2 128
 constexpr int kVecPerLayer = 1280;               // packed fp32: bqkv 384, bo, b1, b2, ln1 g/b, ln2 g/b
 constexpr int kTilesPerLayer = 6;                // weight tiles: Q, K, V, O, FFN-in, FFN-out
+// Stacks of up to kVecSmemLayers layers keep every layer's biases and
+// LayerNorm affines (and the final affine) in shared memory, copied once by
+// the row warps, so the per-chunk parameter reads of the row passes are
+// shared-memory broadcasts instead of L1 / L2 round trips.
+constexpr int kVecSmemLayers = 5;
+constexpr int kVecSmemBytes = (kVecSmemLayers * kVecPerLayer + 2 * kD) * 4;
 
 struct Params {
   const float* x;          // [B, S, 128] fp32
@@ -71,7 +77,8 @@ struct Cfg {
   static constexpr int OFF_Q = 3 * kTileBytes;
   static constexpr int OFF_K = 4 * kTileBytes;
   static constexpr int OFF_V = 5 * kTileBytes;
-  static constexpr int SMEM_BYTES = 6 * kTileBytes + 1024;
+  static constexpr int OFF_VEC = 6 * kTileBytes;          // parameter vectors (short stacks)
+  static constexpr int SMEM_BYTES = 6 * kTileBytes + kVecSmemBytes + 1024;
 };
 
 enum : unsigned { kSiteA = 1, kSiteW = 2, kSiteAcc = 3, kSiteQkv = 4, kSiteS = 5, kSiteP = 6, kSitePv = 7,
@@ -83,9 +90,10 @@ __device__ __forceinline__ uint32_t swz_unit(int r, int u, int units) {
   return units == 8 ? (u ^ (r & 7)) : (u ^ ((r >> 1) & 3));
 }
 
-// Four consecutive fp32 parameters (bias, LayerNorm affine) through the
-// read-only path; every thread of the CTA reads the same addresses.
-__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+// Four consecutive fp32 parameters (bias, LayerNorm affine); every thread of
+// the CTA reads the same addresses, in shared memory (short stacks) or in
+// global memory (generic load: the pointer may be either).
+__device__ __forceinline__ float4 ldg4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
 // 32 fp32 values of this thread's TMEM lane from column t.
 __device__ __forceinline__ void tmem_chunk(uint32_t t, float (&v)[32]) {
@@ -403,6 +411,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       return true;
     };
+    // Parameter vectors: copied into shared memory by the 128 row threads
+    // (then a barrier of those 4 warps only, reached by all of them before
+    // any wait that could end early), or read from global memory.
+    const float* vbase = p.vec;
+    const float* fgp = p.final_g;
+    const float* fbp = p.final_b;
+    if (p.L <= kVecSmemLayers) {
+      float* sv = reinterpret_cast<float*>(smem + C::OFF_VEC);
+      const int n4 = p.L * kVecPerLayer / 4;
+      for (int i = r; i < n4; i += kRows) reinterpret_cast<float4*>(sv)[i] = reinterpret_cast<const float4*>(p.vec)[i];
+      float* sg = sv + kVecSmemLayers * kVecPerLayer;
+      if (r < kD / 4) {
+        reinterpret_cast<float4*>(sg)[r] = reinterpret_cast<const float4*>(p.final_g)[r];
+        reinterpret_cast<float4*>(sg + kD)[r] = reinterpret_cast<const float4*>(p.final_b)[r];
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kRows) : "memory");
+      vbase = sv;
+      fgp = sg;
+      fbp = sg + kD;
+    }
     // The residual stream lives in TMEM (columns [0, 128) of this thread's
     // lane); every pass over a row goes 32 columns at a time.
     const uint32_t t_x = t_lane + kColX;
@@ -421,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_store_chunk(t_x + q * 32, v);
     }
     tmem_st_wait();
-    ln_tmem_to_a(t_x, p.vec + 768, p.vec + 896, p.eps, sA, r);
+    ln_tmem_to_a(t_x, vbase + 768, vbase + 896, p.eps, sA, r);
     signal(&a_ready);
     // x += bias + acc, unless `keep` (the row keeps x); `zero` clears the row.
     auto residual = [&](const float* bias, bool keep, bool zero) {
@@ -446,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
     };
     for (int l = 0; l < p.L && ok; ++l) {
-      const float* vec = p.vec + static_cast<int64_t>(l) * kVecPerLayer;
+      const float* vec = vbase + static_cast<int64_t>(l) * kVecPerLayer;
       // ---- q | k | v: + bias, fp16, into the per-head tiles ----
       if (!wait_acc()) break;
       // the 12 chunks of the q | k | v accumulators are contiguous in TMEM
@@ -606,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 8; ++c) {
             float4 o;
             const int gc = q * 32 + 4 * c;
-            const float4 fg = ldg4(p.final_g + gc), fb = ldg4(p.final_b + gc);
+            const float4 fg = ldg4(fgp + gc), fb = ldg4(fbp + gc);
             o.x = (v[4 * c] - mean) * rstd * fg.x + fb.x;
             o.y = (v[4 * c + 1] - mean) * rstd * fg.y + fb.y;
             o.z = (v[4 * c + 2] - mean) * rstd * fg.z + fb.z;
