@@ -727,6 +727,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  // The weights are not written by the previous kernel: the W halves of the
+  // first tile's first stages are requested before waiting for it, so their
+  // latency overlaps its tail under programmatic dependent launch. The
+  // stages' full barriers expect both halves; A follows after the wait.
+  const int w_early = blockIdx.x < num_tiles ? min(C::STAGES, k_blocks) : 0;
+  if (warp == 0 && lane == 0) {
+    const int n0 = (static_cast<int>(blockIdx.x) % n_tiles) * BN;
+    for (int s = 0; s < w_early; ++s) {
+      mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+      tma_load_2d(smem + s * C::STAGE_BYTES + C::A_BYTES, &map_w, &full_bar[s], s * kBK, n0);
+    }
+  }
   grid_dep_wait();  // the previous kernel's outputs are complete and visible
 
   if (warp == 0) {
@@ -735,10 +747,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int issued = 0;  // stages issued so far; the first w_early already hold W
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * kBM;
         const int n0 = (tile % n_tiles) * BN;
-        for (int kb = 0; kb < k_blocks; ++kb) {
+        for (int kb = 0; kb < k_blocks; ++kb, ++issued) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, &abort_flag, p.wait_limit_ns)) {
             report_error(kDevWaitTimeout, kid * 256 + kSiteEmpty);
             abort_flag = 1;
@@ -747,9 +760,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
-          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+          if (issued >= w_early) {
+            mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+            tma_load_2d(sb, &map_w, &full_bar[stage], kb * kBK, n0);
+          }
           tma_load_2d(sa, &map_a, &full_bar[stage], kb * kBK, m0);
-          tma_load_2d(sb, &map_w, &full_bar[stage], kb * kBK, n0);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
