@@ -520,30 +520,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t t_s = t_lane + kColAcc + b * 128;
-        // pass 1: row max over the valid keys
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        auto s_col = [t_s](int q) { return t_s + q * 32; };
-        tmem_pipeline(q_end, s_col, [&](uint32_t(&v)[32], int q) {
+        // The row's scores (up to 128 keys, q_end 32-key chunks, warp-uniform)
+        // come out of TMEM with one round of loads and one wait; then the
+        // row max over the valid keys, and P = 2^(s*c - m*c) packed fp16 over
+        // the scores already read.
+        uint32_t sv[4][32];
 #pragma unroll
-          for (int k = 0; k < 32; ++k)
-            mx4[k & 3] = fmaxf(mx4[k & 3], q * 32 + k < lim ? __uint_as_float(v[k]) : -INFINITY);
-        });
+        for (int q = 0; q < 4; ++q)
+          if (q < q_end) tmem_ld32(t_s + q * 32, sv[q]);
+        // one wait; each call names its chunk's registers, so no use of them
+        // can be scheduled above it
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (q < q_end) tmem_ld_wait(sv[q]);
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (q < q_end) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+              mx4[k & 3] = fmaxf(mx4[k & 3], q * 32 + k < lim ? __uint_as_float(sv[q][k]) : -INFINITY);
+          }
         const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         const float neg_mc = (mx == -INFINITY) ? 0.f : -mx * sl;
-        // pass 2: P = 2^(s*c - m*c), packed fp16 over the scores already read
         float ls4[4] = {0.f, 0.f, 0.f, 0.f};
-        tmem_pipeline(q_end, s_col, [&](uint32_t(&v)[32], int q) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (q >= q_end) continue;
           uint32_t w[16];
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
             const int c = q * 32 + k;
-            const float e0 = (c < lim) ? ex2_approx(fmaf(__uint_as_float(v[k]), sl, neg_mc)) : 0.f;
-            const float e1 = (c + 1 < lim) ? ex2_approx(fmaf(__uint_as_float(v[k + 1]), sl, neg_mc)) : 0.f;
+            const float e0 = (c < lim) ? ex2_approx(fmaf(__uint_as_float(sv[q][k]), sl, neg_mc)) : 0.f;
+            const float e1 = (c + 1 < lim) ? ex2_approx(fmaf(__uint_as_float(sv[q][k + 1]), sl, neg_mc)) : 0.f;
             ls4[(k >> 1) & 3] += e0 + e1;
             w[k / 2] = pack_half2(e0, e1);
           }
           tmem_st16(t_s + q * 16, w);  // P over scores this thread has already read
-        });
+        }
 #pragma unroll 1
         for (int q = q_end; q < 4; ++q) {
           uint32_t w[16];
