@@ -455,9 +455,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto residual = [&](const float* bias, bool keep, bool zero) {
 #pragma unroll 1
       for (int q = 0; q < 4; ++q) {
-        float v[32], a[32];
-        tmem_chunk(t_x + q * 32, v);
-        tmem_chunk(t_lane + kColAcc + q * 32, a);
+        // x and the accumulator chunk with one wait
+        uint32_t xr[32], ar[32];
+        tmem_ld32(t_x + q * 32, xr);
+        tmem_ld32(t_lane + kColAcc + q * 32, ar);
+        tmem_ld_wait(xr);
+        tmem_ld_wait(ar);
+        float v[32];
 #pragma unroll
         for (int k4 = 0; k4 < 8; ++k4) {
           const float4 bq = ldg4(bias + q * 32 + 4 * k4);
@@ -465,7 +469,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int k = 4 * k4 + j;
-            const float y = keep ? v[k] : v[k] + (a[k] + bb[j]);
+            const float xk = __uint_as_float(xr[k]);
+            const float y = keep ? xk : xk + (__uint_as_float(ar[k]) + bb[j]);
             v[k] = zero ? 0.f : y;
           }
         }
