@@ -585,11 +585,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int h = 0; h < H; ++h) {
         const float il = row_pad ? 0.f : inv_l_sh[h][r];
-#pragma unroll 1
+        // the head's HD columns of O with one round of loads and one wait
+        uint32_t oh[HD / 16][16];
+#pragma unroll
+        for (int q = 0; q < HD / 16; ++q) tmem_ld16(t_lane + kColO + h * HD + q * 16, oh[q]);
+#pragma unroll
+        for (int q = 0; q < HD / 16; ++q) tmem_ld_wait(oh[q]);
+#pragma unroll
         for (int q = 0; q < HD / 16; ++q) {
-          uint32_t o[16];
-          tmem_ld16(t_lane + kColO + h * HD + q * 16, o);
-          tmem_ld_wait(o);
+          const uint32_t* o = oh[q];
           const int c = h * HD + q * 16;  // ctx column
           uint32_t w[8];
 #pragma unroll
